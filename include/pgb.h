@@ -1,0 +1,168 @@
+/*
+ * pgb.h - C ABI of the B200-native tensor-parallel linear path.
+ *
+ * One shared library (libpgb.so) exports every entry point below with plain
+ * pointers, sizes and a CUDA stream handle (cudaStream_t passed as void*).
+ * No torch or tvm-ffi types cross this boundary; the Python mirror of the
+ * reference's layers (pico-sglang_b200/) binds it with ctypes.
+ *
+ * Reference interfaces each entry point replaces are cited as
+ * <file>:<line> relative to the reference project root (dakingffo/pico-sglang).
+ *
+ * Errors. Every function returns PGB_OK (0) or a PGB_ERR_* code and records
+ * a message retrievable with pgb_last_error() on the calling thread. This
+ * replaces the reference's C++ PanicError / runtime_assert / NCCL_CHECK /
+ * CUDA_CHECK exceptions (csrc/include/picosgl/utils.hpp:72-173); the Python
+ * wrapper turns a non-zero code into an exception carrying that message.
+ *
+ * Streams. Work is enqueued on the given stream and never synchronises the
+ * host, so calls can be captured into CUDA graphs (engine/graph.py:135-136),
+ * except where a function says otherwise.
+ */
+#ifndef PGB_H_
+#define PGB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PGB_API __attribute__((visibility("default")))
+#else
+#define PGB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PGB_OK 0
+#define PGB_ERR_INVALID 1     /* bad argument: shape, dtype, alignment, pointer */
+#define PGB_ERR_CUDA 2        /* a CUDA runtime or driver call failed */
+#define PGB_ERR_TIMEOUT 3     /* a bounded device-side wait ran out (peer or pipeline) */
+#define PGB_ERR_UNSUPPORTED 4 /* valid request this build does not implement */
+#define PGB_ERR_STATE 5       /* object not ready, uid mismatch, peers not opened */
+
+/* Element types (the three dtypes the reference communicator accepts,
+ * csrc/src/pynccl.cu:60-65). */
+#define PGB_F16 0
+#define PGB_BF16 1
+#define PGB_F32 2
+
+/* Reduction ops (csrc/src/pynccl.cu:44-47). Only sum is on the hot path. */
+#define PGB_OP_SUM 0
+
+#define PGB_UID_BYTES 128     /* NCCL_UNIQUE_ID_BYTES, csrc/src/pynccl.cu:29-31 */
+#define PGB_MAX_RANKS 8
+
+/* Message of the last failed call on this thread ("" if none). */
+PGB_API const char* pgb_last_error(void);
+
+/* ABI version of this library (major * 100 + minor). */
+PGB_API int pgb_version(void);
+
+/* ------------------------------------------------------------------ comm --
+ * Communicator: replaces NCCLWrapper (csrc/src/pynccl.cu:74-196) and the
+ * PyNCCLCommunicator protocol (python/picosgl/distributed/pynccl.py:16-19).
+ * Cross-GPU buffers are one device allocation per rank, exported with CUDA
+ * IPC and opened by every peer; the fused kernels store into peers' buffers
+ * over NVLink and synchronise with epoch flags and bounded waits.
+ */
+typedef struct pgb_comm pgb_comm;
+
+/* Fill out[PGB_UID_BYTES] with a fresh session id. Replaces create_nccl_uid
+ * (csrc/src/pynccl.cu:38-42,207). Rank 0 creates it; the host broadcasts it
+ * over the CPU group as init_pynccl does (python/picosgl/distributed/pynccl.py:53-66). */
+PGB_API int pgb_create_uid(uint8_t* out);
+
+/* Create this rank's side of a communicator on CUDA device `device`.
+ * max_bytes bounds one all_reduce payload served from the internal buffer,
+ * as the reference's max_size_bytes (csrc/src/pynccl.cu:76-93,
+ * engine/engine.py:225-227). world_size == 1 is valid (no peers to open).
+ * Replaces NCCLWrapper::NCCLWrapper (csrc/src/pynccl.cu:76-93). */
+PGB_API int pgb_comm_create(int rank, int world_size, size_t max_bytes, const uint8_t* uid, int device,
+                    pgb_comm** out);
+
+/* Bytes of one exported peer handle. */
+PGB_API int pgb_comm_handle_size(void);
+
+/* Export this rank's buffer handle into out[pgb_comm_handle_size()]. */
+PGB_API int pgb_comm_export_handle(pgb_comm* comm, const void* unused, uint8_t* out);
+
+/* Open every peer's buffer. handles holds world_size handles in rank order
+ * (this rank's own entry is ignored). Checks that every peer was created
+ * with the same uid, world size and layout; fails with PGB_ERR_STATE if not.
+ * Synchronises the device. */
+PGB_API int pgb_comm_open_peers(pgb_comm* comm, const uint8_t* handles);
+
+/* Release peers, buffers and state. Synchronises the device. */
+PGB_API int pgb_comm_destroy(pgb_comm* comm);
+
+/* Budget of every device-side wait on a peer (default 30 s). */
+PGB_API int pgb_comm_set_timeout_ns(pgb_comm* comm, uint64_t ns);
+
+/* Read the device status word (0 = ok, else PGB_ERR_TIMEOUT etc. as the
+ * device recorded it); reset it to 0 when reset != 0. Synchronises the
+ * device. */
+PGB_API int pgb_comm_get_status(pgb_comm* comm, int* out, int reset);
+
+/* This rank's internal buffer of max_bytes bytes (device pointer).
+ * Replaces NCCLWrapper::get_buffer (csrc/src/pynccl.cu:181-183). */
+PGB_API int pgb_comm_get_buffer(pgb_comm* comm, void** out);
+
+/* In-place all-reduce of count elements at data (CUDA, contiguous).
+ * Replaces NCCLWrapper::all_reduce (csrc/src/pynccl.cu:95-137). */
+PGB_API int pgb_all_reduce(pgb_comm* comm, void* data, size_t count, int dtype, int op, void* stream);
+
+/* out[world_size * count] = concatenation of every rank's in[count], rank 0
+ * first. Replaces NCCLWrapper::all_gather (csrc/src/pynccl.cu:139-179). */
+PGB_API int pgb_all_gather(pgb_comm* comm, void* out, const void* in, size_t count, int dtype,
+                   void* stream);
+
+/* --------------------------------------------------------------- linears --
+ * Column-parallel GEMM: y[T, N] = x[T, K] . w[N, K]^T (+ bias[N]).
+ * x, w, y row-major, element type dtype (PGB_BF16 or PGB_F16), f32
+ * accumulation, K % 8 == 0, N % 8 == 0. workspace is split-K scratch of at
+ * least pgb_col_gemm_workspace_size(T, N, K) bytes, zero-filled once when it
+ * is allocated (the kernels leave it zeroed again). Replaces
+ * LinearTPImpl.forward = F.linear (python/picosgl/layers/linear.py:23-27) for
+ * LinearColParallelMerged / LinearColParallelPartitioned (linear.py:45-73). */
+PGB_API size_t pgb_col_gemm_workspace_size(int T, int N, int K);
+PGB_API int pgb_col_gemm(const void* x, const void* w, const void* bias, void* y, int T, int N, int K,
+                 int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Row-parallel GEMM fused with the all-reduce and the residual-add + RMSNorm
+ * that consumes it:
+ *   p_r      = x_local[T, K_local] . w_local[N, K_local]^T (+ bias) on rank r
+ *   y        = sum_r p_r                         (over the communicator)
+ *   s        = y + residual                      (f32)
+ *   residual = s                                 (in place, dtype)
+ *   out      = s * rsqrt(mean(s^2) + eps) * norm_w
+ * Replaces LinearRowParallel.forward (python/picosgl/layers/linear.py:90-97)
+ * -> NCCLWrapper::all_reduce (csrc/src/pynccl.cu:95-137) -> RMSNormFused.forward
+ * with a residual (python/picosgl/layers/norm.py:56-75). With norm_w == NULL
+ * the kernel stops after the reduction and writes y to out (residual unused),
+ * which is LinearRowParallel.forward alone. out may alias nothing else.
+ * Returns PGB_ERR_INVALID for shapes the communicator's buffer cannot hold. */
+PGB_API int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_local, const void* w_local,
+                                   const void* bias, void* residual, const void* norm_w,
+                                   float eps, void* out, int T, int N, int K_local, int dtype,
+                                   void* stream);
+
+/* ----------------------------------------------------------------- norms --
+ * In-place residual-add + RMSNorm: residual = x + residual; x = rmsnorm(residual) * w.
+ * The FlashInfer fused_add_rmsnorm semantics used by RMSNormFused.forward
+ * (python/picosgl/layers/norm.py:74): the sum is normalised in f32 and
+ * stored into residual rounded to dtype. */
+PGB_API int pgb_fused_add_rmsnorm(void* x, void* residual, const void* w, float eps, int T, int H,
+                          int dtype, void* stream);
+
+/* out = rmsnorm(x) * w (x unchanged); RMSNormFused.forward with residual None
+ * (python/picosgl/layers/norm.py:71-72). */
+PGB_API int pgb_rmsnorm(const void* x, const void* w, float eps, void* out, int T, int H, int dtype,
+                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PGB_H_ */

@@ -1,0 +1,46 @@
+// host_common.h - host-side helpers shared by the C-ABI translation units:
+// thread-local last-error string, CUDA error mapping, TMA descriptor
+// encoding through the driver entry point, and device properties.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/pgb.h"
+
+namespace pgb {
+
+// Record a formatted message as this thread's last error and return code.
+int set_error(int code, const char* fmt, ...);
+// Map a CUDA runtime error to PGB_ERR_CUDA with a message naming the call site.
+int cuda_error(cudaError_t e, const char* what);
+
+#define PGB_CUDA_TRY(expr)                                  \
+  do {                                                      \
+    cudaError_t _e = (expr);                                \
+    if (_e != cudaSuccess) return ::pgb::cuda_error(_e, #expr); \
+  } while (0)
+
+struct DeviceInfo {
+  int device;
+  int sm_count;
+  int max_smem_optin;
+  int cc_major, cc_minor;
+};
+// Cached per-device properties of the current device.
+int current_device_info(DeviceInfo* out);
+
+// Encode a 2-D tiled tensor map for a row-major [outer, inner] matrix of
+// 16-bit elements with 128-byte swizzle and zero fill out of bounds.
+int make_tmap_2d_16bit(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                       uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                       bool is_bf16);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace pgb

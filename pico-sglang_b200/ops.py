@@ -1,0 +1,106 @@
+"""Torch-level wrappers over the C ABI.
+
+These functions take CUDA tensors, check them the way the reference's
+TensorMatcher / runtime_assert checks do (csrc/include/picosgl/tensor.hpp,
+csrc/src/pynccl.cu:95-100), and enqueue the sm_100a kernels on the current
+torch stream. There is no CPU path: a missing library or a non-CUDA tensor
+raises.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float16: _lib.PGB_F16, torch.bfloat16: _lib.PGB_BF16, torch.float32: _lib.PGB_F32}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float16, bfloat16 or float32") from None
+
+
+def _require_cuda(name: str, t: torch.Tensor) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device})")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+class _Workspaces:
+    """Per-device zero-initialised scratch for split-K partials and tile counters.
+
+    Grows outside CUDA-graph capture; inside a capture the size must already be
+    sufficient (allocation during capture would not be replayed)."""
+
+    def __init__(self) -> None:
+        self._bufs: dict[int, torch.Tensor] = {}
+        self._lock = threading.Lock()
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        with self._lock:
+            buf = self._bufs.get(idx)
+            if buf is None or buf.numel() < nbytes:
+                if torch.cuda.is_current_stream_capturing():
+                    raise RuntimeError(
+                        f"split-K workspace of {nbytes} bytes needed during CUDA-graph capture; "
+                        "run the same shapes once before capturing"
+                    )
+                size = max(nbytes, 1 << 20)
+                buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
+                self._bufs[idx] = buf
+            return buf
+
+
+WORKSPACES = _Workspaces()
+
+
+def col_gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x . w^T (+ bias) on the tcgen05 kernel; x [T, K], w [N, K]."""
+    _require_cuda("x", x)
+    _require_cuda("weight", w)
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} weight {tuple(w.shape)}")
+    if x.dtype != w.dtype:
+        raise TypeError(f"x {x.dtype} and weight {w.dtype} differ")
+    T, K = x.shape
+    N = w.shape[0]
+    if bias is not None:
+        _require_cuda("bias", bias)
+        if bias.shape != (N,) or bias.dtype != x.dtype:
+            raise ValueError("bias must be [N] with the input dtype")
+    if out is None:
+        out = torch.empty((T, N), dtype=x.dtype, device=x.device)
+    else:
+        _require_cuda("out", out)
+        if out.shape != (T, N) or out.dtype != x.dtype:
+            raise ValueError("out must be [T, N] with the input dtype")
+    lib = _lib.load()
+    need = lib.pgb_col_gemm_workspace_size(T, N, K)
+    ws = WORKSPACES.get(x.device, need)
+    _lib.call(
+        "pgb_col_gemm",
+        x.data_ptr(),
+        w.data_ptr(),
+        bias.data_ptr() if bias is not None else None,
+        out.data_ptr(),
+        T,
+        N,
+        K,
+        dtype_code(x),
+        ws.data_ptr(),
+        ws.numel(),
+        _stream(x),
+    )
+    return out

@@ -1,0 +1,147 @@
+"""Pin the CPU oracle (oracle/) before trusting it.
+
+1. Against golden vectors produced by the reference's own Python layers
+   (tests/golden/make_golden.py): BASELINE config 1 at world_size 2 over
+   gloo, and TP 1/2/4 shards of the row- and column-parallel layers.
+2. Against the known answers of the reference communicator test
+   (tests/distributed/test_pynccl.py:95-148).
+3. Against properties of RMSNorm the reference relies on.
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def tp_small():
+    return dict(np.load(GOLD / "tp_small.npz"))
+
+
+def test_round_to_bf16_matches_torch():
+    g = torch.Generator().manual_seed(3)
+    a = torch.randn(10000, generator=g) * 100
+    a[:5] = torch.tensor([0.0, -0.0, 1e-40, 3.0e38, float("inf")])
+    ref = a.to(torch.bfloat16).float().numpy()
+    got = oracle.round_to(a.numpy(), "bf16")
+    assert np.array_equal(got, ref)
+    ref16 = a.clamp(-6e4, 6e4).half().float().numpy()
+    assert np.array_equal(oracle.round_to(a.clamp(-6e4, 6e4).numpy(), "f16"), ref16)
+
+
+def test_cfg1_row_parallel_matches_reference_gloo():
+    """Config 1: reference LinearRowParallel, world_size 2, gloo all_reduce, f32."""
+    gold = np.load(GOLD / "cfg1.npz")
+    torch.manual_seed(0)
+    x = torch.randn(64, 4096).numpy()
+    W = (torch.randn(4096, 4096) * 0.02).numpy()
+    residual = torch.randn(64, 4096).numpy()
+    out, res, y = oracle.row_parallel_addnorm(x, W, residual, np.ones(4096, np.float32), 1e-6, n=2,
+                                              dtype="f32")
+    rel = np.abs(y - gold["y"]).max() / np.abs(gold["y"]).max()
+    assert rel < 1e-5, rel
+    rel = np.abs(out - gold["out_restated"]).max() / np.abs(gold["out_restated"]).max()
+    assert rel < 1e-5, rel
+    assert np.abs(res - gold["residual_out"]).max() / np.abs(gold["residual_out"]).max() < 1e-5
+
+
+@pytest.mark.parametrize("n", [1, 2, 4])
+def test_row_parallel_partials_match_reference(tp_small, n):
+    x = tp_small["x_i"]
+    w = tp_small["w_down"]
+    for r in range(n):
+        w_r, x_r = oracle.row_shard(w, x, r, n)
+        got32 = oracle.linear(x_r, w_r, dtype="f32")
+        ref32 = tp_small[f"row_f32_tp{n}_r{r}"]
+        assert np.abs(got32 - ref32).max() <= 1e-5 * np.abs(ref32).max()
+        xb, wb = oracle.round_to(x_r, "bf16"), oracle.round_to(w_r, "bf16")
+        gotb = oracle.linear(xb, wb, dtype="bf16")
+        refb = tp_small[f"row_bf16_tp{n}_r{r}"]
+        # Both round one f32-class accumulation to bf16: at most one ulp apart.
+        assert np.abs(gotb - refb).max() <= 2 ** -7 * np.abs(refb).max()
+    # TP partial sums reproduce TP=1 (tests/mtp/test_tp2_numeric.py:175-188 bar: 1e-3).
+    full = tp_small["row_f32_tp1_r0"]
+    summed = oracle.all_reduce_sum([tp_small[f"row_f32_tp{n}_r{r}"] for r in range(n)], "f32")
+    err = np.abs(summed - full).max()
+    assert err < 1e-3 and err / np.abs(full).max() < 1e-3
+
+
+@pytest.mark.parametrize("n", [1, 2, 4])
+def test_column_parallel_shards_match_reference_loader(tp_small, n):
+    for r in range(n):
+        w_gu = oracle.col_shard_merged([tp_small["w_gate"], tp_small["w_up"]], r, n)
+        assert np.array_equal(w_gu, tp_small[f"gateup_w_tp{n}_r{r}"])
+        w_qkv = oracle.col_shard_partitioned(tp_small["wq"], tp_small["wk"], tp_small["wv"],
+                                             num_kv_heads=2, rank=r, n=n)
+        assert np.array_equal(w_qkv, tp_small[f"qkv_w_tp{n}_r{r}"])
+        y = oracle.linear(tp_small["x_h"], w_gu, dtype="f32")
+        ref = tp_small[f"gateup_f32_tp{n}_r{r}"]
+        assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+        y = oracle.linear(tp_small["x_h"], w_qkv, dtype="f32")
+        ref = tp_small[f"qkv_f32_tp{n}_r{r}"]
+        assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_all_reduce_known_answers(tp):
+    """tests/distributed/test_pynccl.py:95-134, restated for the oracle."""
+    K = 512
+    x = np.ones(8192 * K // 64, np.float32)
+    for _ in range(4):
+        x = oracle.all_reduce_sum([x] * tp, "f16")
+    assert np.all(x == tp ** 4)
+    x = oracle.all_reduce_sum([np.full(1024, r, np.float32) for r in range(tp)], "f16")
+    assert np.all(x == tp * (tp - 1) // 2)
+    half = np.concatenate([np.zeros(512, np.float32), np.ones(512, np.float32)])
+    x = oracle.all_reduce_sum([half] * tp, "f16")
+    assert np.all(x[:512] == 0) and np.all(x[512:] == tp)
+
+
+def test_fused_add_rmsnorm_properties():
+    g = np.random.default_rng(5)
+    x = g.standard_normal((16, 512)).astype(np.float32)
+    r = g.standard_normal((16, 512)).astype(np.float32)
+    w = np.ones(512, np.float32)
+    out, res = oracle.fused_add_rmsnorm(x, r, w, 1e-6, "f32")
+    np.testing.assert_allclose(res, x + r, rtol=0, atol=0)
+    np.testing.assert_allclose(np.sqrt((out.astype(np.float64) ** 2).mean(-1)), 1.0, rtol=1e-5)
+    # Scale invariance of RMSNorm (eps negligible).
+    out2, _ = oracle.fused_add_rmsnorm(4 * x, 4 * r, w, 1e-12, "f32")
+    np.testing.assert_allclose(out2, out, rtol=1e-5, atol=1e-6)
+    # bf16 mode: residual is the rounded f32 sum; the norm uses the unrounded sum.
+    outb, resb = oracle.fused_add_rmsnorm(oracle.round_to(x, "bf16"), oracle.round_to(r, "bf16"),
+                                          w, 1e-6, "bf16")
+    s = oracle.round_to(x, "bf16") + oracle.round_to(r, "bf16")
+    assert np.array_equal(resb, oracle.round_to(s, "bf16"))
+    # rmsnorm without residual
+    o = oracle.rmsnorm(x, w, 1e-6, "f32")
+    np.testing.assert_allclose(np.sqrt((o.astype(np.float64) ** 2).mean(-1)), 1.0, rtol=1e-5)
+
+
+def test_tp_layer_step_sharded_equals_unsharded():
+    """Row-parallel sums over n ranks reproduce the TP=1 layer (f32 mode)."""
+    g = np.random.default_rng(9)
+    H, I, T = 128, 256, 4
+    wts = {
+        "qkv": g.standard_normal((192, H)).astype(np.float32) * 0.02,
+        "o": g.standard_normal((H, H)).astype(np.float32) * 0.02,
+        "gate_up": g.standard_normal((2 * I, H)).astype(np.float32) * 0.02,
+        "down": g.standard_normal((H, I)).astype(np.float32) * 0.02,
+        "ln1": np.ones(H, np.float32),
+        "ln2": np.ones(H, np.float32),
+    }
+    h, a = (g.standard_normal((T, H)).astype(np.float32) for _ in range(2))
+    m = g.standard_normal((T, I)).astype(np.float32)
+    res = g.standard_normal((T, H)).astype(np.float32)
+    one = oracle.tp_layer_step(h, a, m, res, wts, 1e-6, n=1, dtype="f32")
+    four = oracle.tp_layer_step(h, a, m, res, wts, 1e-6, n=4, rank=2, dtype="f32")
+    for k in ("x1", "r1", "x2", "r2"):
+        np.testing.assert_allclose(four[k], one[k], rtol=1e-5, atol=1e-5)
