@@ -8,8 +8,17 @@ The directory name contains a hyphen, so import it with
 ``importlib.import_module("pico-sglang_b200")``.
 """
 
-from . import _lib
+from . import _lib, ops
 from ._lib import PGBError, PGBTimeout
-from .ops import col_gemm
+from .ops import col_gemm, fused_add_rmsnorm, rmsnorm, row_gemm_allreduce_addnorm
 
-__all__ = ["PGBError", "PGBTimeout", "_lib", "col_gemm"]
+__all__ = [
+    "PGBError",
+    "PGBTimeout",
+    "_lib",
+    "col_gemm",
+    "fused_add_rmsnorm",
+    "ops",
+    "rmsnorm",
+    "row_gemm_allreduce_addnorm",
+]

@@ -1,0 +1,156 @@
+// norm.cu - standalone RMSNorm kernels for the norms that are not fused
+// into a row-parallel GEMM: the first layer's input_layernorm (residual is
+// None, python/picosgl/layers/norm.py:71-72) and any fused_add_rmsnorm whose
+// producer is not a row-parallel layer (norm.py:73-75).
+//
+// One CTA per row, 8-element vectors, f32 statistics; the semantics of
+// FlashInfer's RMSNormKernel / FusedAddRMSNormKernel (norm.cuh:387-470):
+// the f32 sum x + residual is normalised and stored into residual rounded.
+#include "host_common.h"
+#include "reduce_phases.cuh"
+
+namespace pgb {
+
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxVec = 8;  // width <= 256 * 64 = 16384
+
+template <typename IO>
+__global__ void __launch_bounds__(kNormThreads) fused_add_rmsnorm_kernel(IO* x, IO* residual,
+                                                                         const IO* w, float eps,
+                                                                         int width) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int nvec = width >> 3;
+  float s[kNormMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+      float a[8], r[8];
+      load8<IO>(x + static_cast<size_t>(t) * width + v * 8, a);
+      load8<IO>(residual + static_cast<size_t>(t) * width + v * 8, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        s[i][j] = a[j] + r[j];
+        ss += s[i][j] * s[i][j];
+      }
+    }
+  }
+  const float rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+      const size_t off = static_cast<size_t>(t) * width + v * 8;
+      float wv[8], o[8];
+      load8<IO>(w + v * 8, wv);
+      store8<IO>(residual + off, s[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = s[i][j] * rcp * wv[j];
+      store8<IO>(x + off, o);
+    }
+  }
+}
+
+template <typename IO>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const IO* x, const IO* w, float eps,
+                                                               IO* out, int width) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int nvec = width >> 3;
+  float s[kNormMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+      load8<IO>(x + static_cast<size_t>(t) * width + v * 8, s[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += s[i][j] * s[i][j];
+    }
+  }
+  const float rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+      float wv[8], o[8];
+      load8<IO>(w + v * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = s[i][j] * rcp * wv[j];
+      store8<IO>(out + static_cast<size_t>(t) * width + v * 8, o);
+    }
+  }
+}
+
+namespace {
+int check_norm_args(const char* what, int T, int H, int dtype, const void* a, const void* b,
+                    const void* c) {
+  if (T < 0 || H <= 0) return set_error(PGB_ERR_INVALID, "%s: bad shape T=%d H=%d", what, T, H);
+  if (H % 8 != 0) return set_error(PGB_ERR_INVALID, "%s: hidden size %d not a multiple of 8", what, H);
+  if (H > kNormThreads * 8 * kNormMaxVec)
+    return set_error(PGB_ERR_UNSUPPORTED, "%s: hidden size %d above %d", what, H,
+                     kNormThreads * 8 * kNormMaxVec);
+  if (dtype != PGB_BF16 && dtype != PGB_F16 && dtype != PGB_F32)
+    return set_error(PGB_ERR_INVALID, "%s: unknown dtype %d", what, dtype);
+  const uintptr_t m = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                      reinterpret_cast<uintptr_t>(c);
+  if (a == nullptr || b == nullptr || c == nullptr)
+    return set_error(PGB_ERR_INVALID, "%s: null pointer argument", what);
+  if ((m & 15u) != 0u) return set_error(PGB_ERR_INVALID, "%s: pointers must be 16-byte aligned", what);
+  return PGB_OK;
+}
+}  // namespace
+
+}  // namespace pgb
+
+extern "C" int pgb_fused_add_rmsnorm(void* x, void* residual, const void* w, float eps, int T,
+                                     int H, int dtype, void* stream) {
+  using namespace pgb;
+  int rc = check_norm_args("fused_add_rmsnorm", T, H, dtype, x, residual, w);
+  if (rc || T == 0) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PGB_BF16:
+      fused_add_rmsnorm_kernel<__nv_bfloat16><<<T, kNormThreads, 0, s>>>(
+          static_cast<__nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
+          static_cast<const __nv_bfloat16*>(w), eps, H);
+      break;
+    case PGB_F16:
+      fused_add_rmsnorm_kernel<__half><<<T, kNormThreads, 0, s>>>(
+          static_cast<__half*>(x), static_cast<__half*>(residual), static_cast<const __half*>(w), eps, H);
+      break;
+    default:
+      fused_add_rmsnorm_kernel<float><<<T, kNormThreads, 0, s>>>(
+          static_cast<float*>(x), static_cast<float*>(residual), static_cast<const float*>(w), eps, H);
+  }
+  PGB_CUDA_TRY(cudaGetLastError());
+  return PGB_OK;
+}
+
+extern "C" int pgb_rmsnorm(const void* x, const void* w, float eps, void* out, int T, int H,
+                           int dtype, void* stream) {
+  using namespace pgb;
+  int rc = check_norm_args("rmsnorm", T, H, dtype, x, w, out);
+  if (rc || T == 0) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case PGB_BF16:
+      rmsnorm_kernel<__nv_bfloat16><<<T, kNormThreads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), eps,
+          static_cast<__nv_bfloat16*>(out), H);
+      break;
+    case PGB_F16:
+      rmsnorm_kernel<__half><<<T, kNormThreads, 0, s>>>(static_cast<const __half*>(x),
+                                                       static_cast<const __half*>(w), eps,
+                                                       static_cast<__half*>(out), H);
+      break;
+    default:
+      rmsnorm_kernel<float><<<T, kNormThreads, 0, s>>>(static_cast<const float*>(x),
+                                                      static_cast<const float*>(w), eps,
+                                                      static_cast<float*>(out), H);
+  }
+  PGB_CUDA_TRY(cudaGetLastError());
+  return PGB_OK;
+}

@@ -1,0 +1,295 @@
+// reduce_phases.cuh - grid-wide cross-rank barrier and the reduce / add /
+// RMSNorm / gather phases that follow the partial pushes.
+//
+// Kernels using these are launched cooperatively (all CTAs co-resident),
+// because CTAs wait on the arrival of every other CTA of the grid.
+#pragma once
+
+#include "comm.h"
+#include "sm100.cuh"
+
+namespace pgb {
+
+constexpr int kBarPartials = 0;   // every rank pushed its partial rows
+constexpr int kBarResults = 1;    // every row owner pushed its finished rows
+constexpr int kBarFinish = 3;     // local only: last CTA publishes the new epoch
+
+// Epoch of the call this kernel executes.
+__device__ __forceinline__ uint32_t comm_begin(const CommDev& cm) {
+  return ld_acquire_gpu(cm.epoch) + 1u;
+}
+
+// All CTAs of the grid arrive; the last one to arrive publishes this rank's
+// arrival (epoch e) to every rank's flag `bar`; then every CTA waits until
+// all ranks' flags reached e. The wait is bounded by cm.timeout_ns and ends
+// early when another CTA already recorded an error. Every CTA must call this
+// with the same `bar` sequence, errors or not, so counters stay balanced.
+__device__ __forceinline__ bool grid_cross_barrier(const CommDev& cm, int bar, uint32_t e,
+                                                   bool sys_scope) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    if (sys_scope)
+      __threadfence_system();
+    else
+      __threadfence();
+    const uint32_t old = atom_add_acqrel_gpu(&cm.arrive[bar], 1u);
+    if (old == gridDim.x - 1) {
+      cm.arrive[bar] = 0u;
+      if (sys_scope) __threadfence_system();
+      for (int r = 0; r < cm.world; ++r) st_release_sys(&cm.flags[r][bar * PGB_MAX_RANKS + cm.rank], e);
+    }
+    volatile int* st = cm.status;
+    if (*st != 0) ok = 0;
+    Deadline d(cm.timeout_ns);
+    const uint32_t* mine = cm.flags[cm.rank] + bar * PGB_MAX_RANKS;
+    for (int r = 0; r < cm.world && ok; ++r) {
+      while (!epoch_reached(ld_acquire_sys(mine + r), e)) {
+        if (d.expired()) {
+          record_error(cm.status, kDevTimeoutPeer);
+          ok = 0;
+          break;
+        }
+        if ((d.n & 255u) == 0u && *st != 0) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// Last CTA to finish stores the epoch of this call.
+__device__ __forceinline__ void comm_end(const CommDev& cm, uint32_t e) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t old = atom_add_acqrel_gpu(&cm.arrive[kBarFinish], 1u);
+    if (old == gridDim.x - 1) {
+      cm.arrive[kBarFinish] = 0u;
+      st_release_gpu(cm.epoch, e);
+    }
+  }
+}
+
+// Row geometry of a reduction over `rows` rows of `width` elements.
+struct RowSplit {
+  int rows;
+  int oneshot;     // 1: every rank reduces every row; 0: row owners (two-shot)
+  int rows_per;    // two-shot ownership block
+  int rows_cap;    // rows per source rank inside a slot region
+  __device__ __forceinline__ int owner(int t) const { return oneshot ? -1 : t / rows_per; }
+  __device__ __forceinline__ int first(int rank) const { return oneshot ? 0 : min(rows, rank * rows_per); }
+  __device__ __forceinline__ int last(int rank) const {
+    return oneshot ? rows : min(rows, (rank + 1) * rows_per);
+  }
+};
+
+template <typename T>
+struct Vec8;  // 8 elements in 16 (16-bit types) or 32 (f32) bytes
+
+template <typename IO>
+__device__ __forceinline__ void load8(const IO* p, float* v);
+template <typename IO>
+__device__ __forceinline__ void store8(IO* p, const float* v);
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float* v) {
+  const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = __uint_as_float(w[j] << 16);
+    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float* v) {
+  const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __half22float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float* v) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldcg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float* v) {
+  uint4 u;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __nv_bfloat162 b = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+    w[j] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store8<__half>(__half* p, const float* v) {
+  uint4 u;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    w[j] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* p, const float* v) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Round f32 values to the representable values of IO (the reduced output is
+// materialised in IO precision in the reference before the norm reads it).
+template <typename IO>
+__device__ __forceinline__ float round_io(float v);
+template <>
+__device__ __forceinline__ float round_io<__nv_bfloat16>(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+template <>
+__device__ __forceinline__ float round_io<__half>(float v) {
+  return __half2float(__float2half_rn(v));
+}
+template <>
+__device__ __forceinline__ float round_io<float>(float v) {
+  return v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red /* >= 32 floats */) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return t;
+}
+
+// Phase 2 for one row: sum the world partials of row t, then either write
+// the sum (do_norm == 0) or residual-add + RMSNorm it. Writes out[t] and
+// residual[t] locally and, for two-shot, pushes both rows to every peer's
+// result region. MAXV bounds the 8-element vectors per thread.
+template <typename IO, typename SlotT, int MAXV>
+__device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity,
+                                           int t, int width, IO* out, IO* residual,
+                                           const IO* norm_w, float eps, int do_norm,
+                                           float* red) {
+  const int nvec = width >> 3;
+  const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
+  const SlotT* slot0 = reinterpret_cast<const SlotT*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes);
+  const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
+  float s[MAXV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[i][j] = 0.f;
+      for (int src = 0; src < cm.world; ++src) {
+        float p[8];
+        load8<SlotT>(slot0 + src * src_stride + static_cast<size_t>(lr) * width + v * 8, p);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[i][j] += p[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[i][j] = round_io<IO>(s[i][j]);
+      if (do_norm) {
+        float r[8];
+        load8<IO>(residual + static_cast<size_t>(t) * width + v * 8, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          s[i][j] += r[j];
+          ss += s[i][j] * s[i][j];
+        }
+      }
+    }
+  }
+  float rcp = 1.f;
+  if (do_norm) rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
+  const bool push = !rs.oneshot && cm.world > 1;
+  IO* res_planes[PGB_MAX_RANKS];
+  IO* out_planes[PGB_MAX_RANKS];
+  if (push) {
+    for (int d = 0; d < cm.world; ++d) {
+      uint8_t* base = cm.results[d] + parity * cm.result_parity_bytes;
+      out_planes[d] = reinterpret_cast<IO*>(base);
+      res_planes[d] = reinterpret_cast<IO*>(base + cm.result_parity_bytes / 2);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * blockDim.x;
+    if (v < nvec) {
+      const size_t off = static_cast<size_t>(t) * width + v * 8;
+      float o[8];
+      if (do_norm) {
+        float w[8];
+        load8<IO>(norm_w + v * 8, w);
+        store8<IO>(residual + off, s[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = s[i][j] * rcp * w[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = s[i][j];
+      }
+      store8<IO>(out + off, o);
+      if (push) {
+        for (int d = 0; d < cm.world; ++d) {
+          if (d == cm.rank) continue;
+          store8<IO>(out_planes[d] + off, o);
+          if (do_norm) store8<IO>(res_planes[d] + off, s[i]);
+        }
+      }
+    }
+  }
+}
+
+// Phase 3 (two-shot): copy the rows owned by other ranks from this rank's
+// result region into out / residual.
+template <typename IO>
+__device__ __forceinline__ void gather_rows(const CommDev& cm, const RowSplit& rs, uint32_t parity,
+                                            int width, IO* out, IO* residual, int do_norm) {
+  const uint8_t* base = cm.results[cm.rank] + parity * cm.result_parity_bytes;
+  const IO* out_plane = reinterpret_cast<const IO*>(base);
+  const IO* res_plane = reinterpret_cast<const IO*>(base + cm.result_parity_bytes / 2);
+  const int r0 = rs.first(cm.rank), r1 = rs.last(cm.rank);
+  const int nvec = width >> 3;
+  const long long total = static_cast<long long>(rs.rows) * nvec;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / nvec);
+    if (t >= r0 && t < r1) continue;
+    const size_t off = static_cast<size_t>(t) * width + (i % nvec) * 8;
+    constexpr int kU4 = static_cast<int>(sizeof(IO)) / 2;  // 16-byte words per 8 elements
+#pragma unroll
+    for (int k = 0; k < kU4; ++k) {
+      reinterpret_cast<uint4*>(out + off)[k] = __ldcg(reinterpret_cast<const uint4*>(out_plane + off) + k);
+      if (do_norm)
+        reinterpret_cast<uint4*>(residual + off)[k] =
+            __ldcg(reinterpret_cast<const uint4*>(res_plane + off) + k);
+    }
+  }
+}
+
+}  // namespace pgb

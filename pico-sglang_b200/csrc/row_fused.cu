@@ -1,0 +1,368 @@
+// row_fused.cu - row-parallel GEMM + all-reduce + residual-add + RMSNorm in
+// one cooperative kernel.
+//
+// Replaces, per call, the reference sequence
+//   LinearRowParallel.forward   y = F.linear(x_local, W_local)         (layers/linear.py:90-97)
+//   -> all_reduce(y, "sum")     memcpy + ncclAllReduce + memcpy        (csrc/src/pynccl.cu:95-137)
+//   -> RMSNormFused.forward     flashinfer fused_add_rmsnorm           (layers/norm.py:73-75)
+//
+// Phase 1 (tcgen05 GEMM, persistent): each finished output tile (split-K
+//   combined on this GPU) is rounded to the I/O type and stored straight
+//   from registers into the slot region of the rank(s) that reduce its rows:
+//   every rank for one-shot, the row owner for two-shot. Remote stores go
+//   over NVLink while later tiles are still being multiplied.
+// Barrier 0: grid arrival, then a release flag to every rank, then bounded
+//   waits for all ranks' flags of this epoch.
+// Phase 2: per owned row, sum the ranks' partials in rank order (f32),
+//   round to the I/O type (the reference materialises the reduced tensor),
+//   add the residual, store the residual, RMS-normalise and store out.
+//   Two-shot owners also push both rows to every peer's result region.
+// Barrier 1 + phase 3 (two-shot only): copy the other owners' rows in.
+#include "comm.h"
+#include "gemm_plan.h"
+#include "gemm_sm100.cuh"
+#include "host_common.h"
+#include "reduce_phases.cuh"
+
+namespace pgb {
+
+constexpr int kRowMaxVec = 8;  // 8 vectors of 8 per thread: width <= 192 * 64 = 12288
+
+struct RowArgs {
+  GemmShape g;
+  CommDev cm;
+  RowSplit rs;
+  void* out;
+  void* residual;
+  const void* norm_w;
+  const void* bias;
+  float eps;
+  int do_norm;
+};
+
+template <typename IO>
+__device__ __forceinline__ void row_store_partial(const RowArgs& a, uint32_t parity, int t, int n,
+                                                  IO val) {
+  const int H = a.g.N;
+  const size_t src_off = static_cast<size_t>(a.cm.rank) * a.rs.rows_cap * H;
+  if (a.rs.oneshot) {
+    for (int d = 0; d < a.cm.world; ++d) {
+      IO* base = reinterpret_cast<IO*>(a.cm.slots[d] + parity * a.cm.slot_parity_bytes);
+      base[src_off + static_cast<size_t>(t) * H + n] = val;
+    }
+  } else {
+    const int o = t / a.rs.rows_per;
+    IO* base = reinterpret_cast<IO*>(a.cm.slots[o] + parity * a.cm.slot_parity_bytes);
+    base[src_off + static_cast<size_t>(t - o * a.rs.rows_per) * H + n] = val;
+  }
+}
+
+template <typename IO>
+__device__ __forceinline__ void row_store_partial_vec32(const RowArgs& a, uint32_t parity, int t,
+                                                        int n0, const float* v) {
+  const int H = a.g.N;
+  const size_t src_off = static_cast<size_t>(a.cm.rank) * a.rs.rows_cap * H;
+  uint4 pk[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) pk[j] = pack8<IO>(v + 8 * j);
+  int d0 = 0, d1 = a.cm.world;
+  size_t row = static_cast<size_t>(t);
+  if (!a.rs.oneshot) {
+    d0 = t / a.rs.rows_per;
+    d1 = d0 + 1;
+    row = static_cast<size_t>(t - d0 * a.rs.rows_per);
+  }
+  for (int d = d0; d < d1; ++d) {
+    IO* base = reinterpret_cast<IO*>(a.cm.slots[d] + parity * a.cm.slot_parity_bytes);
+    uint4* dst = reinterpret_cast<uint4*>(base + src_off + row * H + n0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[j] = pk[j];
+  }
+}
+
+template <typename IO, int BN, bool SWAP, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    row_fused_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     RowArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t s_epoch;
+  __shared__ float s_red[32];
+  GemmCtl c = gemm_carve_smem<BN, STAGES>(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const GemmShape& g = a.g;
+
+  if (threadIdx.x == 0) {
+    s_epoch = comm_begin(a.cm);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&c.full[i], 1);
+      mbar_init(&c.empty[i], 1);
+    }
+    mbar_init(&c.acc_full[0], 1);
+    mbar_init(&c.acc_full[1], 1);
+    mbar_init(&c.acc_empty[0], kEpiThreads);
+    mbar_init(&c.acc_empty[1], kEpiThreads);
+    mbar_init(c.drain, 1);
+    *c.abort = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(c.tmem_base, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t e = s_epoch;
+  const uint32_t parity = e & 1u;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t hw = l2_policy_evict_first();
+      const uint64_t hx = l2_policy_evict_last();
+      gemm_producer<BN, STAGES>(g, c, &tm_a, &tm_b, SWAP ? hw : hx, SWAP ? hx : hw);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) gemm_mma<BN, STAGES>(g, c, umma_idesc_f16(kTileP, BN, std::is_same<IO, __nv_bfloat16>::value));
+  } else {
+    const uint32_t tmem = *c.tmem_base;
+    const int row = epi_row();
+    const IO* bias = static_cast<const IO*>(a.bias);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int unit = blockIdx.x; unit < g.num_units; unit += gridDim.x) {
+      const TileCoord tc = decode_unit(g, unit);
+      if (!mbar_wait(&c.acc_full[acc], acc_phase, g.wait_ns, c.abort)) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+        break;
+      }
+      tc_fence_after();
+      bool owner = true;
+      if (g.splits > 1) owner = splitk_publish<BN>(g, c, tc, tmem, acc);
+      if (owner) {
+#pragma unroll 1
+        for (int col = 0; col < BN; col += 32) {
+          float v[32];
+          epi_load_chunk<BN>(g, tc, tmem, acc, col, v);
+          if constexpr (SWAP) {
+            const int n = tc.p * kTileP + row;
+            const int t0 = tc.q * BN + col;
+            if (n < g.N) {
+              const float b = bias != nullptr ? io_to_f32<IO>(bias[n]) : 0.f;
+#pragma unroll 4
+              for (int j = 0; j < 32; ++j) {
+                const int t = t0 + j;
+                if (t < g.T) row_store_partial<IO>(a, parity, t, n, f32_to_io<IO>(v[j] + b));
+              }
+            }
+          } else {
+            const int t = tc.p * kTileP + row;
+            const int n0 = tc.q * BN + col;
+            if (t < g.T) {
+              if (bias != nullptr) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (n0 + j < g.N) v[j] += io_to_f32<IO>(bias[n0 + j]);
+              }
+              if (n0 + 32 <= g.N) {
+                row_store_partial_vec32<IO>(a, parity, t, n0, v);
+              } else {
+                for (int j = 0; j < 32 && n0 + j < g.N; ++j)
+                  row_store_partial<IO>(a, parity, t, n0 + j, f32_to_io<IO>(v[j]));
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&c.acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(*c.tmem_base, 2 * BN);
+  }
+
+  const bool multi = a.cm.world > 1;
+  // A pipeline timeout anywhere on this GPU poisons the status; the barrier
+  // then stops waiting and phase 2 is skipped.
+  const bool ok = grid_cross_barrier(a.cm, kBarPartials, e, multi);
+  IO* out = static_cast<IO*>(a.out);
+  IO* residual = static_cast<IO*>(a.residual);
+  const IO* norm_w = static_cast<const IO*>(a.norm_w);
+  if (ok) {
+    const int r0 = a.rs.first(a.cm.rank), r1 = a.rs.last(a.cm.rank);
+    for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x)
+      reduce_row<IO, IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps,
+                                     a.do_norm, s_red);
+  }
+  if (multi && !a.rs.oneshot) {
+    const bool ok2 = grid_cross_barrier(a.cm, kBarResults, e, true);
+    if (ok && ok2) gather_rows<IO>(a.cm, a.rs, parity, g.N, out, residual, a.do_norm);
+  }
+  comm_end(a.cm, e);
+}
+
+namespace {
+
+template <int BN>
+constexpr int row_stages() {
+  return (224 * 1024) / (kTileP * kBlockK * 2 + BN * kBlockK * 2) > 12
+             ? 12
+             : (224 * 1024) / (kTileP * kBlockK * 2 + BN * kBlockK * 2);
+}
+
+template <typename IO, int BN, bool SWAP>
+int launch_row(pgb_comm* c, RowArgs args, const void* x, const void* w, cudaStream_t stream) {
+  constexpr int STAGES = row_stages<BN>();
+  using L = GemmSmem<BN, STAGES>;
+  static_assert(L::kBytes + 256 <= 232448, "shared memory budget");
+  auto kern = row_fused_kernel<IO, BN, SWAP, STAGES>;
+  PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
+  const int T = args.g.T, N = args.g.N, K = args.g.K;
+  CUtensorMap tm_x, tm_w;
+  int rc = make_tmap_2d_16bit(&tm_x, x, K, T, static_cast<uint64_t>(K) * 2, kBlockK,
+                              SWAP ? BN : kTileP, kBf16);
+  if (rc) return rc;
+  rc = make_tmap_2d_16bit(&tm_w, w, K, N, static_cast<uint64_t>(K) * 2, kBlockK,
+                          SWAP ? kTileP : BN, kBf16);
+  if (rc) return rc;
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(c->sm_count);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const CUtensorMap& ta = SWAP ? tm_w : tm_x;
+  const CUtensorMap& tb = SWAP ? tm_x : tm_w;
+  PGB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
+  return PGB_OK;
+}
+
+template <typename IO>
+int dispatch_row(pgb_comm* c, const GemmPlan& p, const RowArgs& args, const void* x, const void* w,
+                 cudaStream_t s) {
+  if (!p.swap) return launch_row<IO, 256, false>(c, args, x, w, s);
+  switch (p.bn) {
+    case 32: return launch_row<IO, 32, true>(c, args, x, w, s);
+    case 64: return launch_row<IO, 64, true>(c, args, x, w, s);
+    case 128: return launch_row<IO, 128, true>(c, args, x, w, s);
+    case 256: return launch_row<IO, 256, true>(c, args, x, w, s);
+    default: return set_error(PGB_ERR_INVALID, "no kernel for tile width %d", p.bn);
+  }
+}
+
+}  // namespace
+
+// Choose one-shot or two-shot for a reduction of `rows` x `width` elements of
+// `elem` bytes; returns false if neither fits the communicator buffers.
+bool plan_rows(const pgb_comm* c, int rows, int width, int elem, RowSplit* rs) {
+  const double row_bytes = static_cast<double>(width) * elem;
+  const double S = row_bytes * rows;
+  const int n = c->world;
+  const bool one_fits = static_cast<double>(n) * S <= static_cast<double>(c->slot_parity_bytes);
+  const int rows_per = (rows + n - 1) / n;
+  const bool two_fits = static_cast<double>(n) * rows_per * row_bytes <= c->slot_parity_bytes &&
+                        2.0 * S <= static_cast<double>(c->result_parity_bytes);
+  bool one = (n == 1) || !two_fits;
+  if (n > 1 && one_fits && two_fits) {
+    // NVLink ~770 GB/s per direction, HBM ~6.5 TB/s, one extra barrier ~2 us.
+    const double t_one = (n - 1) * S / 770e9 + n * S / 6.5e12;
+    const double t_two = 2.0 * (n - 1) / n * S / 770e9 + S / 6.5e12 + 2e-6;
+    one = t_one <= t_two;
+  }
+  if (one && !one_fits) return false;
+  rs->rows = rows;
+  rs->oneshot = one ? 1 : 0;
+  rs->rows_per = one ? rows : rows_per;
+  rs->rows_cap = one ? rows : rows_per;
+  return true;
+}
+
+}  // namespace pgb
+
+extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_local,
+                                              const void* w_local, const void* bias,
+                                              void* residual, const void* norm_w, float eps,
+                                              void* out, int T, int N, int K_local, int dtype,
+                                              void* stream) {
+  using namespace pgb;
+  if (comm == nullptr) return set_error(PGB_ERR_INVALID, "row_gemm: null communicator");
+  if (comm->world > 1 && !comm->peers_open)
+    return set_error(PGB_ERR_STATE, "row_gemm: peers not opened (call pgb_comm_open_peers)");
+  if (T < 0 || N <= 0 || K_local <= 0)
+    return set_error(PGB_ERR_INVALID, "row_gemm: bad shape T=%d N=%d K=%d", T, N, K_local);
+  if (T == 0) return PGB_OK;
+  if (dtype == PGB_F32)
+    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: f32 is served by the check-mode path");
+  if (dtype != PGB_BF16 && dtype != PGB_F16)
+    return set_error(PGB_ERR_INVALID, "row_gemm: unknown dtype %d", dtype);
+  if (K_local % 8 != 0 || N % 8 != 0)
+    return set_error(PGB_ERR_INVALID, "row_gemm: K=%d and N=%d must be multiples of 8", K_local, N);
+  if (N > kGemmThreads * 8 * kRowMaxVec)
+    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: hidden size %d above %d", N,
+                     kGemmThreads * 8 * kRowMaxVec);
+  if (x_local == nullptr || w_local == nullptr || out == nullptr)
+    return set_error(PGB_ERR_INVALID, "row_gemm: null pointer argument");
+  if (norm_w != nullptr && residual == nullptr)
+    return set_error(PGB_ERR_INVALID, "row_gemm: norm weight given without residual");
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual) |
+                        reinterpret_cast<uintptr_t>(norm_w);
+  if ((mis & 15u) != 0u)
+    return set_error(PGB_ERR_INVALID, "row_gemm: out / residual / norm weight not 16-byte aligned");
+  int cur = -1;
+  PGB_CUDA_TRY(cudaGetDevice(&cur));
+  if (cur != comm->device)
+    return set_error(PGB_ERR_INVALID, "row_gemm: current device %d, communicator on %d", cur,
+                     comm->device);
+
+  RowSplit rs;
+  if (!plan_rows(comm, T, N, 2, &rs))
+    return set_error(PGB_ERR_INVALID,
+                     "row_gemm: %d x %d payload exceeds the communicator buffer (max_bytes=%zu)", T,
+                     N, comm->max_bytes);
+  const GemmPlan p = plan_gemm(T, N, K_local, comm->sm_count, kSplitScratchBytes);
+  if (static_cast<size_t>(p.p_tiles) * p.q_tiles * 4u > kTileCounterBytes)
+    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: too many tiles (%d)", p.p_tiles * p.q_tiles);
+
+  RowArgs args{};
+  args.g.T = T;
+  args.g.N = N;
+  args.g.K = K_local;
+  args.g.kblocks = p.kblocks;
+  args.g.splits = p.splits;
+  args.g.p_tiles = p.p_tiles;
+  args.g.q_tiles = p.q_tiles;
+  args.g.num_units = p.units;
+  args.g.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
+  args.g.tile_counters = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kCounters);
+  args.g.ws = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
+  args.g.wait_ns = 2000000000ull;
+  args.cm = comm_dev(comm);
+  args.rs = rs;
+  args.out = out;
+  args.residual = residual;
+  args.norm_w = norm_w;
+  args.bias = bias;
+  args.eps = eps;
+  args.do_norm = norm_w != nullptr ? 1 : 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == PGB_BF16) return dispatch_row<__nv_bfloat16>(comm, p, args, x_local, w_local, s);
+  return dispatch_row<__half>(comm, p, args, x_local, w_local, s);
+}

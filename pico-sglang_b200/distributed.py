@@ -1,0 +1,266 @@
+"""Communicator and TP plumbing mirroring python/picosgl/distributed/.
+
+- ``PGBCommunicator`` satisfies the reference's ``PyNCCLCommunicator``
+  protocol (distributed/pynccl.py:16-19): ``all_reduce(input, "sum")`` in
+  place, ``all_gather(output, input)``, ``get_buffer()``. It is constructed
+  like ``NCCLWrapper`` (rank, world_size, max_bytes, uid; csrc/src/pynccl.cu:76-93)
+  and backed by libpgb's IPC peer buffers instead of an NCCL communicator.
+- ``init_comm`` follows ``init_pynccl`` (distributed/pynccl.py:39-71): rank 0
+  creates the uid, it is broadcast over the CPU (gloo) group, then the peer
+  handles are exchanged over the same group and opened.
+- ``DistributedCommunicator`` / ``PGBDistributedImpl`` mirror the class-level
+  plug point of distributed/impl.py:34-62, and ``DistributedInfo`` /
+  ``set_tp_info`` / ``get_tp_info`` mirror distributed/info.py:7-46.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from abc import ABC, abstractmethod
+from contextlib import contextmanager
+from dataclasses import dataclass
+from typing import Literal
+
+import torch
+
+from . import _lib
+from .ops import _require_cuda, _stream, dtype_code
+
+# ------------------------------------------------------------------ TP info --
+
+
+@dataclass(frozen=True)
+class DistributedInfo:
+    """Rank and size of the tensor-parallel group (distributed/info.py:7-16)."""
+
+    rank: int
+    size: int
+
+    def __post_init__(self):
+        assert 0 <= self.rank < self.size
+
+    def is_primary(self) -> bool:
+        return self.rank == 0
+
+
+_TP_INFO: DistributedInfo | None = None
+
+
+def set_tp_info(tp_info: DistributedInfo) -> None:
+    global _TP_INFO
+    assert _TP_INFO is None, "TP info has been set"
+    _TP_INFO = tp_info
+
+
+def get_tp_info() -> DistributedInfo:
+    assert _TP_INFO is not None, "TP info has not been set"
+    return _TP_INFO
+
+
+def try_get_tp_info() -> DistributedInfo | None:
+    return _TP_INFO
+
+
+@contextmanager
+def tp_override(tp_info: DistributedInfo):
+    global _TP_INFO
+    saved = _TP_INFO
+    _TP_INFO = tp_info
+    try:
+        yield
+    finally:
+        _TP_INFO = saved
+
+
+# ------------------------------------------------------------- communicator --
+
+
+def create_uid() -> bytes:
+    """128 random bytes identifying one communicator (replaces create_nccl_uid)."""
+    buf = (ctypes.c_uint8 * _lib.UID_BYTES)()
+    _lib.call("pgb_create_uid", buf)
+    return bytes(buf)
+
+
+class PGBCommunicator:
+    """libpgb communicator for one rank; see module docstring."""
+
+    def __init__(self, rank: int, world_size: int, max_bytes: int, uid: bytes | list[int],
+                 device: int | None = None):
+        if isinstance(uid, (list, tuple)):
+            uid = bytes((v & 0xFF) for v in uid)
+        if len(uid) != _lib.UID_BYTES:
+            raise ValueError(f"uid must be {_lib.UID_BYTES} bytes, got {len(uid)}")
+        if device is None:
+            device = torch.cuda.current_device()
+        self.rank = rank
+        self.world_size = world_size
+        self.max_bytes = max_bytes
+        self.device = device
+        handle = ctypes.c_void_p()
+        ubuf = (ctypes.c_uint8 * _lib.UID_BYTES).from_buffer_copy(uid)
+        _lib.call("pgb_comm_create", rank, world_size, max_bytes, ubuf, device, ctypes.byref(handle))
+        self._h = handle
+        self._closed = False
+
+    # -- peer exchange ------------------------------------------------------
+    def export_handle(self) -> bytes:
+        n = _lib.load().pgb_comm_handle_size()
+        buf = (ctypes.c_uint8 * n)()
+        _lib.call("pgb_comm_export_handle", self._h, None, buf)
+        return bytes(buf)
+
+    def open_peers(self, handles: list[bytes]) -> None:
+        if len(handles) != self.world_size:
+            raise ValueError(f"expected {self.world_size} handles, got {len(handles)}")
+        blob = b"".join(handles)
+        buf = (ctypes.c_uint8 * len(blob)).from_buffer_copy(blob)
+        _lib.call("pgb_comm_open_peers", self._h, buf)
+
+    # -- PyNCCLCommunicator protocol ---------------------------------------
+    def all_reduce(self, input: torch.Tensor, op: Literal["sum"] = "sum") -> None:
+        _require_cuda("input", input)
+        if op != "sum":
+            raise ValueError(f"unsupported reduce op {op!r}")
+        _lib.call("pgb_all_reduce", self._h, input.data_ptr(), input.numel(), dtype_code(input),
+                  _lib.PGB_OP_SUM, _stream(input))
+
+    def all_gather(self, output: torch.Tensor, input: torch.Tensor) -> None:
+        _require_cuda("input", input)
+        _require_cuda("output", output)
+        if output.size(0) != input.size(0) * self.world_size:
+            raise ValueError("Destination tensor has incorrect size")
+        if output.dtype != input.dtype or output.numel() != input.numel() * self.world_size:
+            raise ValueError("output must hold world_size copies of input's shape and dtype")
+        _lib.call("pgb_all_gather", self._h, output.data_ptr(), input.data_ptr(), input.numel(),
+                  dtype_code(input), _stream(input))
+
+    def get_buffer(self) -> ctypes.c_void_p:
+        out = ctypes.c_void_p()
+        _lib.call("pgb_comm_get_buffer", self._h, ctypes.byref(out))
+        return out
+
+    # -- health -------------------------------------------------------------
+    def set_timeout(self, seconds: float) -> None:
+        _lib.call("pgb_comm_set_timeout_ns", self._h, int(seconds * 1e9))
+
+    def check_status(self, reset: bool = True) -> None:
+        """Synchronise and raise PGBTimeout if a device-side wait ran out."""
+        st = ctypes.c_int()
+        _lib.call("pgb_comm_get_status", self._h, ctypes.byref(st), int(reset))
+        if st.value:
+            raise _lib.PGBTimeout(st.value, "communicator", "a bounded wait on a peer or the pipeline ran out; "
+                                  "the communicator must be destroyed and re-created")
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        if self._closed:
+            raise RuntimeError("communicator closed")
+        return self._h
+
+    def close(self) -> None:
+        if not self._closed:
+            self._closed = True
+            _lib.call("pgb_comm_destroy", self._h)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def init_comm(*, tp_rank: int, tp_size: int, tp_cpu_group, max_size_bytes: int = 0,
+              device: int | None = None) -> PGBCommunicator:
+    """Create and connect a communicator over the CPU group (init_pynccl, pynccl.py:39-71)."""
+    import torch.distributed as dist
+
+    ids = [create_uid()] if tp_rank == 0 else [None]
+    if tp_size > 1:
+        dist.broadcast_object_list(ids, src=0, group=tp_cpu_group)
+    uid = ids[0]
+    assert uid is not None, f"Failed to get communicator uid on {tp_rank = }"
+    comm = PGBCommunicator(tp_rank, tp_size, max_size_bytes, uid, device)
+    if tp_size > 1:
+        handles: list = [None] * tp_size
+        dist.all_gather_object(handles, comm.export_handle(), group=tp_cpu_group)
+        comm.open_peers(handles)
+        dist.barrier(group=tp_cpu_group)
+    return comm
+
+
+# ---------------------------------------------------- impl plug-in point --
+
+
+class DistributedImpl(ABC):
+    @abstractmethod
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor: ...
+
+    @abstractmethod
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor: ...
+
+
+class NoopDistributedImpl(DistributedImpl):
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+
+@dataclass
+class PGBDistributedImpl(DistributedImpl):
+    """PyNCCLDistributedImpl (impl.py:34-50) over a PGBCommunicator."""
+
+    comm: PGBCommunicator
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        self.comm.all_reduce(x, "sum")
+        return x
+
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        world = self.comm.world_size
+        shape = list(x.shape)
+        shape[0] *= world
+        result = x.new_empty(shape)
+        self.comm.all_gather(result, x)
+        return result
+
+
+class DistributedCommunicator:
+    impl: DistributedImpl = NoopDistributedImpl()
+    # The libpgb communicator used by the fused row-parallel kernels (None
+    # until enable_pgb_distributed or set_local_comm ran).
+    comm: PGBCommunicator | None = None
+
+    @classmethod
+    def all_reduce(cls, x: torch.Tensor) -> torch.Tensor:
+        return cls.impl.all_reduce(x)
+
+    @classmethod
+    def all_gather(cls, x: torch.Tensor) -> torch.Tensor:
+        return cls.impl.all_gather(x)
+
+
+def enable_pgb_distributed(tp_info: DistributedInfo, tp_cpu_group, max_bytes: int) -> PGBCommunicator:
+    """enable_pynccl_distributed (impl.py:65-80) for the libpgb communicator."""
+    comm = init_comm(tp_rank=tp_info.rank, tp_size=tp_info.size, tp_cpu_group=tp_cpu_group,
+                     max_size_bytes=max_bytes)
+    DistributedCommunicator.impl = PGBDistributedImpl(comm=comm)
+    DistributedCommunicator.comm = comm
+    return comm
+
+
+def local_comm(max_bytes: int = 64 << 20) -> PGBCommunicator:
+    """Single-rank communicator for TP=1: the fused row kernel still needs its
+    slot buffer and counters."""
+    if DistributedCommunicator.comm is None:
+        DistributedCommunicator.comm = PGBCommunicator(0, 1, max_bytes, create_uid())
+    return DistributedCommunicator.comm
+
+
+def destroy_distributed() -> None:
+    if DistributedCommunicator.comm is not None:
+        DistributedCommunicator.comm.close()
+    DistributedCommunicator.comm = None
+    DistributedCommunicator.impl = NoopDistributedImpl()

@@ -1,0 +1,207 @@
+"""Drop-in mirrors of the reference's TP linear layers and fused RMSNorm.
+
+Constructor signatures, attribute names (``weight`` / ``bias``, found by the
+loader through BaseOP.state_dict, python/picosgl/layers/base.py:14-59) and
+local shard sizes are those of python/picosgl/layers/linear.py:11-97 and
+norm.py:56-75; ``forward`` runs the libpgb kernels.
+
+Fusing a row-parallel layer with the norm that consumes it. The reference's
+decoder layer (models/llama.py:77-86) calls, in order,
+``x, residual = input_layernorm(x, residual)`` -> attention ... ``o_proj(x)``
+-> ``x, residual = post_attention_layernorm(x, residual)`` -> mlp ...
+``down_proj(x)`` -> the next layer's ``input_layernorm`` (or the final
+``norm``). ``link_norm`` ties a row-parallel layer to its consumer. Every
+RMSNormFused.forward records the residual it returns; a linked
+LinearRowParallel.forward then runs GEMM + all-reduce + residual-add + norm
+in one kernel on that residual (in place) and returns the normalised output,
+remembered as already normalised for that norm and residual. The consumer's
+forward recognises it and returns ``(x, residual)`` unchanged. The model
+code does not change, the stream order is the same, and CUDA-graph capture
+records the same single kernel.
+"""
+
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import ops
+from .distributed import DistributedCommunicator, get_tp_info, local_comm
+
+
+def div_even(a: int, b: int, allow_replicate: bool = False) -> int:
+    """utils/misc.py:20-26."""
+    if allow_replicate and b > a:
+        assert b % a == 0, f"{b = } must be divisible by {a = } for KV head replication"
+        return 1
+    assert a % b == 0, f"{a = } must be divisible by {b = }"
+    return a // b
+
+
+class BaseOP:
+    """Attribute-walking state dict of layers/base.py:14-59."""
+
+    def state_dict(self, *, prefix: str = "", result: dict | None = None) -> dict:
+        result = result if result is not None else {}
+        for name, param in self.__dict__.items():
+            if name.startswith("_"):
+                continue
+            key = f"{prefix}.{name}" if prefix else name
+            if isinstance(param, torch.Tensor):
+                result[key] = param
+            elif isinstance(param, BaseOP):
+                param.state_dict(prefix=key, result=result)
+        return result
+
+    def load_state_dict(self, state_dict: dict, *, prefix: str = "", _internal: bool = False) -> None:
+        for name, param in self.__dict__.items():
+            if name.startswith("_"):
+                continue
+            key = f"{prefix}.{name}" if prefix else name
+            if isinstance(param, torch.Tensor):
+                item = state_dict.pop(key)
+                assert param.shape == item.shape, f"shape mismatch for {key}: {param.shape} vs {item.shape}"
+                setattr(self, name, item.to(param.dtype))
+            elif isinstance(param, BaseOP):
+                param.load_state_dict(state_dict, prefix=key, _internal=True)
+        if not _internal and state_dict:
+            raise RuntimeError(f"Unexpected keys in state_dict: {list(state_dict.keys())}")
+
+
+class _FuseContext(threading.local):
+    def __init__(self) -> None:
+        self.residual: torch.Tensor | None = None
+        self.fused: tuple | None = None  # (out, norm, residual) produced by a linked row layer
+
+
+_CTX = _FuseContext()
+
+
+def reset_fusion_context() -> None:
+    _CTX.residual = None
+    _CTX.fused = None
+
+
+def _flat2d(x: torch.Tensor) -> torch.Tensor:
+    return x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+
+
+class LinearTPImpl(BaseOP):
+    """layers/linear.py:11-27, forward on the tcgen05 column GEMM."""
+
+    def __init__(self, input_size: int, output_size: int, has_bias: bool):
+        self.weight = torch.empty(output_size, input_size)
+        self.bias = torch.empty(output_size) if has_bias else None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x2 = _flat2d(x).contiguous()
+        y = ops.col_gemm(x2, self.weight, self.bias)
+        return y.view(*x.shape[:-1], y.shape[-1])
+
+
+class LinearReplicated(LinearTPImpl):
+    pass
+
+
+class LinearColParallelMerged(LinearTPImpl):
+    """linear.py:45-56 (gate_up_proj): local rows [gate/n; up/n]."""
+
+    def __init__(self, input_size: int, output_sizes: list[int], has_bias: bool):
+        tp = get_tp_info()
+        super().__init__(input_size, sum(div_even(s, tp.size) for s in output_sizes), has_bias)
+
+
+class LinearColParallelPartitioned(LinearTPImpl):
+    """linear.py:59-73 (qkv_proj): per-head shards with kv replication."""
+
+    def __init__(self, input_size: int, partition_size: int, partitions: list[tuple[int, bool]],
+                 has_bias: bool):
+        tp = get_tp_info()
+        parts = [div_even(p, tp.size, rep) for p, rep in partitions]
+        super().__init__(input_size, sum(parts) * partition_size, has_bias)
+
+
+class LinearRowParallel(LinearTPImpl):
+    """linear.py:76-97: K-sharded GEMM followed by the sum all-reduce.
+
+    Unlinked, forward returns the reduced output (fused GEMM + all-reduce for
+    TP > 1, the plain GEMM for TP = 1). Linked to its consuming RMSNormFused,
+    forward also applies the residual-add + RMSNorm (module docstring).
+    """
+
+    def __init__(self, input_size: int, output_size: int, has_bias: bool):
+        tp = get_tp_info()
+        self._tp_size = tp.size
+        self._norm: RMSNormFused | None = None
+        super().__init__(div_even(input_size, tp.size), output_size, has_bias)
+
+    def link_norm(self, norm: "RMSNormFused | None") -> None:
+        self._norm = norm
+
+    def _comm(self):
+        c = DistributedCommunicator.comm
+        if c is None:
+            if self._tp_size > 1:
+                raise RuntimeError("TP > 1 needs enable_pgb_distributed() before forward")
+            c = local_comm()
+        return c
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x2 = _flat2d(x).contiguous()
+        T = x2.shape[0]
+        N = self.weight.shape[0]
+        res = _CTX.residual
+        norm = self._norm
+        if norm is not None and res is not None and res.shape == (T, N) and res.dtype == x2.dtype:
+            out = ops.row_gemm_allreduce_addnorm(self._comm(), x2, self.weight, res, norm.weight, norm.eps,
+                                                 bias=self.bias)
+            _CTX.fused = (out, norm, res)
+            return out.view(*x.shape[:-1], N)
+        if self._tp_size == 1:
+            y = ops.col_gemm(x2, self.weight, self.bias)
+        else:
+            y = ops.row_gemm_allreduce_addnorm(self._comm(), x2, self.weight, None, None, 0.0, bias=self.bias)
+        return y.view(*x.shape[:-1], N)
+
+
+class RMSNormFused(BaseOP):
+    """norm.py:56-75 on libpgb kernels, aware of linked row-parallel producers."""
+
+    def __init__(self, size: int, eps: float) -> None:
+        self.eps = eps
+        self.weight = torch.empty(size)
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None):
+        f = _CTX.fused
+        if f is not None and f[0] is x and f[1] is self and f[2] is residual:
+            _CTX.fused = None
+            _CTX.residual = residual
+            return x, residual
+        _CTX.fused = None
+        if residual is None:
+            out = ops.rmsnorm(x, self.weight, self.eps)
+            _CTX.residual = x
+            return out, x
+        ops.fused_add_rmsnorm(x, residual, self.weight, self.eps)
+        _CTX.residual = residual
+        return x, residual
+
+
+def link_fused_norms(layers: list, final_norm: RMSNormFused | None = None) -> int:
+    """Link o_proj -> post_attention_layernorm and down_proj -> the next
+    layer's input_layernorm (the final norm after the last layer), following
+    the decoder wiring of models/llama.py:77-86 and :103-108. Returns the
+    number of links made."""
+    n = 0
+    for i, layer in enumerate(layers):
+        attn = getattr(layer, "self_attn", None)
+        if attn is not None and isinstance(getattr(attn, "o_proj", None), LinearRowParallel):
+            attn.o_proj.link_norm(layer.post_attention_layernorm)
+            n += 1
+        mlp = getattr(layer, "mlp", None)
+        if mlp is not None and isinstance(getattr(mlp, "down_proj", None), LinearRowParallel):
+            nxt = layers[i + 1].input_layernorm if i + 1 < len(layers) else final_norm
+            mlp.down_proj.link_norm(nxt)
+            n += nxt is not None
+    return n

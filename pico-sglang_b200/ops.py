@@ -104,3 +104,70 @@ def col_gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
         _stream(x),
     )
     return out
+
+
+def row_gemm_allreduce_addnorm(comm, x_local: torch.Tensor, w_local: torch.Tensor,
+                               residual: torch.Tensor | None, norm_w: torch.Tensor | None,
+                               eps: float, out: torch.Tensor | None = None,
+                               bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused row-parallel GEMM + all-reduce (+ residual-add + RMSNorm).
+
+    With norm_w: residual <- y + residual (in place), returns rmsnorm(residual) * norm_w.
+    Without: returns y = sum over ranks of x_local . w_local^T.
+    """
+    _require_cuda("x", x_local)
+    _require_cuda("weight", w_local)
+    if x_local.dim() != 2 or w_local.dim() != 2 or x_local.shape[1] != w_local.shape[1]:
+        raise ValueError(f"shape mismatch: x {tuple(x_local.shape)} weight {tuple(w_local.shape)}")
+    T, K = x_local.shape
+    N = w_local.shape[0]
+    for name, t in (("residual", residual), ("norm weight", norm_w), ("bias", bias)):
+        if t is not None:
+            _require_cuda(name, t)
+            if t.dtype != x_local.dtype:
+                raise TypeError(f"{name} dtype {t.dtype} differs from input {x_local.dtype}")
+    if norm_w is not None:
+        if residual is None or residual.shape != (T, N) or norm_w.shape != (N,):
+            raise ValueError("residual must be [T, N] and norm weight [N]")
+    if out is None:
+        out = torch.empty((T, N), dtype=x_local.dtype, device=x_local.device)
+    h = comm.handle if hasattr(comm, "handle") else comm
+    _lib.call(
+        "pgb_row_gemm_allreduce_addnorm",
+        h,
+        x_local.data_ptr(),
+        w_local.data_ptr(),
+        bias.data_ptr() if bias is not None else None,
+        residual.data_ptr() if residual is not None else None,
+        norm_w.data_ptr() if norm_w is not None else None,
+        float(eps),
+        out.data_ptr(),
+        T,
+        N,
+        K,
+        dtype_code(x_local),
+        _stream(x_local),
+    )
+    return out
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float) -> None:
+    """In place: residual <- x + residual; x <- rmsnorm(residual) * weight."""
+    for n, t in (("x", x), ("residual", residual), ("weight", weight)):
+        _require_cuda(n, t)
+    if x.shape != residual.shape or x.shape[-1] != weight.shape[-1]:
+        raise ValueError("x / residual / weight shapes disagree")
+    H = x.shape[-1]
+    _lib.call("pgb_fused_add_rmsnorm", x.data_ptr(), residual.data_ptr(), weight.data_ptr(), float(eps),
+              x.numel() // H, H, dtype_code(x), _stream(x))
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    _require_cuda("x", x)
+    _require_cuda("weight", weight)
+    H = x.shape[-1]
+    if out is None:
+        out = torch.empty_like(x)
+    _lib.call("pgb_rmsnorm", x.data_ptr(), weight.data_ptr(), float(eps), out.data_ptr(), x.numel() // H, H,
+              dtype_code(x), _stream(x))
+    return out

@@ -23,9 +23,13 @@ def _ref(x, w, b=None):
 
 
 def _check(y, ref, tol=2e-2):
+    """|y - ref| <= max(tol * RMS(ref), 1 ulp of the output dtype at ref)."""
+    mant = {torch.bfloat16: 7, torch.float16: 10}[y.dtype]
     rms = ref.pow(2).mean().sqrt().item()
-    err = (y.float() - ref).abs().max().item()
-    assert err <= tol * rms + 1e-6, f"max|diff|={err:.4g} rms={rms:.4g}"
+    d = (y.float() - ref).abs()
+    u = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(1e-30))) - mant)
+    worst = (d / torch.maximum(torch.full_like(d, tol * rms), u)).max().item()
+    assert worst <= 1.0, f"max|diff|={d.max().item():.4g} rms={rms:.4g} worst/bound={worst:.3g}"
 
 
 SHAPES = [

@@ -1,0 +1,221 @@
+"""Multi-GPU communicator and fused row-parallel kernel, one process per GPU.
+
+Mirrors the reference's communicator test (tests/distributed/test_pynccl.py):
+spawned ranks, a gloo CPU group for bootstrap, the same known answers
+(ones reduced four times = tp^4; rank values = n(n-1)/2 with rank 0
+lagging 1 s; half zeros / half ones -> {0, tp}; all_gather of the rank id).
+Then the fused GEMM + all-reduce + residual-add + RMSNorm at TP = n against
+the full-width f32 restatement, one-shot and two-shot sizes, CUDA-graph
+replay, and a bounded timeout when a peer never joins.
+
+Needs at least 2 GPUs; ranks never share a GPU (kernels that wait on one
+another must run on different devices).
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import time
+import traceback
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+EPS = 1e-6
+
+
+def _ngpus() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def _within(a, ref, tol=2e-2):
+    mant = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23}[ref.dtype]
+    rms = ref.float().pow(2).mean().sqrt().item()
+    d = (a.float() - ref.float()).abs()
+    u = torch.exp2(torch.floor(torch.log2(ref.float().abs().clamp_min(1e-30))) - mant)
+    worst = (d / torch.maximum(torch.full_like(d, tol * rms), u)).max().item()
+    return worst <= 1.0, f"max|diff|={d.max().item():.4g} rms={rms:.4g} worst/bound={worst:.3g}"
+
+
+def _worker(rank: int, world: int, port: int, case: str, q):
+    try:
+        sys.path.insert(0, str(ROOT))
+        import importlib
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                init_method=f"tcp://127.0.0.1:{port}", timeout=timedelta(seconds=120))
+        pgb = importlib.import_module("pico-sglang_b200")
+        D = importlib.import_module("pico-sglang_b200.distributed")
+        comm = D.init_comm(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD,
+                           max_size_bytes=64 << 20)
+        dev = torch.device("cuda", rank)
+        out = {}
+        if case == "known_answers":
+            K = 512
+            dtype = torch.float16
+            f = lambda x: comm.all_reduce(x, "sum")  # noqa: E731
+            x = torch.ones(8192 * K, dtype=dtype, device=dev)
+            for _ in range(4):
+                f(x)
+            out["pow"] = bool(torch.all(x == world ** 4).item())
+            x = torch.full((8192 * K,), rank, dtype=dtype, device=dev)
+            if rank == 0:
+                torch.cuda.synchronize()
+                time.sleep(1)
+            f(x)
+            out["lag"] = bool(torch.all(x == world * (world - 1) // 2).item())
+            x = torch.cat([torch.zeros(8192 * K // 2, dtype=dtype, device=dev),
+                           torch.ones(8192 * K // 2, dtype=dtype, device=dev)])
+            f(x)
+            out["half"] = bool(torch.all(x[: 8192 * K // 2] == 0).item() and torch.all(x[8192 * K // 2:] == world).item())
+            for dt in (torch.bfloat16, torch.float32):
+                for n in (1, 7, 1000, 12345):
+                    x = torch.full((n,), float(rank + 1), dtype=dt, device=dev)
+                    f(x)
+                    out[f"small_{dt}_{n}"] = bool(torch.all(x == world * (world + 1) / 2).item())
+            src = torch.full((K,), rank, dtype=dtype, device=dev)
+            dst = torch.empty((K * world,), dtype=dtype, device=dev)
+            comm.all_gather(dst, src)
+            exp = torch.arange(world, dtype=dtype, device=dev).repeat_interleave(K)
+            out["gather"] = bool(torch.equal(dst, exp))
+            comm.check_status()
+        elif case == "fused":
+            for (T, H, K) in ((1, 4096, 4096), (8, 4096, 12288), (64, 4096, 4096), (256, 4096, 12288),
+                              (1000, 4096, 2048), (3, 200, 256)):
+                g = torch.Generator(device=dev).manual_seed(T + H + K)
+                x = torch.randn(T, K, device=dev, generator=g).bfloat16()
+                w = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
+                r = torch.randn(T, H, device=dev, generator=g).bfloat16()
+                nw = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).bfloat16()
+                k = K // world
+                xl = x[:, rank * k:(rank + 1) * k].contiguous()
+                wl = w[:, rank * k:(rank + 1) * k].contiguous()
+                # Reference: per-rank bf16 partials (F.linear), summed, rounded, add-norm.
+                parts = [(x[:, i * k:(i + 1) * k].float() @ w[:, i * k:(i + 1) * k].float().t()).bfloat16()
+                         for i in range(world)]
+                y = torch.stack([p.float() for p in parts]).sum(0).bfloat16()
+                s = y.float() + r.float()
+                ref_r = s.bfloat16()
+                ref = (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + EPS) * nw.float()).bfloat16()
+                rr = r.clone()
+                o = pgb.ops.row_gemm_allreduce_addnorm(comm, xl, wl, rr, nw, EPS)
+                yy = pgb.ops.row_gemm_allreduce_addnorm(comm, xl, wl, None, None, EPS)
+                comm.check_status()
+                out[f"out_{T}_{H}_{K}"] = _within(o, ref)
+                out[f"res_{T}_{H}_{K}"] = _within(rr, ref_r)
+                out[f"y_{T}_{H}_{K}"] = _within(yy, y)
+                # Every rank must hold the identical result (replicated residual stream).
+                gathered = [torch.empty_like(o) for _ in range(world)]
+                objs = [None] * world
+                dist.all_gather_object(objs, (o.float().sum().item(), rr.float().sum().item()))
+                out[f"same_{T}_{H}_{K}"] = (len(set(objs)) == 1, str(objs))
+                del gathered
+            # graph replay
+            T, H, K = 16, 4096, 4096
+            g = torch.Generator(device=dev).manual_seed(5)
+            x = torch.randn(T, K // world, device=dev, generator=g).bfloat16()
+            w = (torch.randn(H, K // world, device=dev, generator=g) * 0.02).bfloat16()
+            r = torch.randn(T, H, device=dev, generator=g).bfloat16()
+            nw = torch.ones(H, device=dev).bfloat16()
+            rr = r.clone()
+            o = torch.empty_like(r)
+            pgb.ops.row_gemm_allreduce_addnorm(comm, x, w, rr, nw, EPS, out=o)
+            torch.cuda.synchronize()
+            first = o.clone()
+            s = torch.cuda.Stream()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s), torch.cuda.graph(graph, stream=s):
+                pgb.ops.row_gemm_allreduce_addnorm(comm, x, w, rr, nw, EPS, out=o)
+            same = True
+            for _ in range(3):
+                rr.copy_(r)
+                torch.cuda.synchronize()
+                dist.barrier()
+                graph.replay()
+                torch.cuda.synchronize()
+                same &= bool(torch.equal(o, first))
+            comm.check_status()
+            del graph
+            out["graph"] = (same, "")
+        elif case == "timeout":
+            comm.set_timeout(0.3)
+            x = torch.ones(4096, dtype=torch.bfloat16, device=dev)
+            raised = False
+            if rank == 0:
+                comm.all_reduce(x, "sum")  # rank 1 never joins
+                try:
+                    comm.check_status()
+                except pgb.PGBTimeout:
+                    raised = True
+            torch.cuda.synchronize()
+            out["raised"] = raised if rank == 0 else True
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, out, None))
+    except Exception:
+        q.put((rank, None, traceback.format_exc()))
+
+
+def _run(world: int, case: str):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + (os.getpid() % 200)
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            rank, out, err = q.get(timeout=300)
+            assert err is None, f"rank {rank} failed:\n{err}"
+            results[rank] = out
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    return results
+
+
+def _worlds():
+    n = _ngpus()
+    return [w for w in (2, 4, 8) if w <= n] or [2]
+
+
+@pytest.mark.parametrize("world", _worlds())
+def test_known_answers(world):
+    if _ngpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, "known_answers")
+    for rank, out in res.items():
+        bad = [k for k, v in out.items() if not v]
+        assert not bad, f"rank {rank}: {bad}"
+
+
+@pytest.mark.parametrize("world", _worlds())
+def test_fused_row_parallel_tp(world):
+    if _ngpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    res = _run(world, "fused")
+    for rank, out in res.items():
+        bad = {k: v[1] for k, v in out.items() if not v[0]}
+        assert not bad, f"rank {rank}: {bad}"
+
+
+def test_peer_timeout_is_reported_not_hung():
+    if _ngpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = _run(2, "timeout")
+    assert res[0]["raised"], "rank 0 did not see a timeout"

@@ -1,0 +1,210 @@
+"""Fused row-parallel GEMM + all-reduce + residual-add + RMSNorm, one rank.
+
+References:
+- a plain torch f32 restatement of the reference sequence
+  F.linear (layers/linear.py:94) -> all_reduce -> fused_add_rmsnorm
+  (layers/norm.py:74): y = bf16(x_f32 . w_f32^T); s = f32(y) + f32(r);
+  r' = bf16(s); out = bf16(s * rsqrt(mean(s^2) + eps) * w_norm);
+- the reference's own library path on the same box: torch F.linear (cuBLAS)
+  followed by flashinfer.fused_add_rmsnorm, the exact calls of
+  LinearRowParallel.forward and RMSNormFused.forward.
+Tolerance (bf16): |diff| <= max(2e-2 * RMS of the reference output, 1 ulp), see within().
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+EPS = 1e-6
+
+
+def torch_ref(x, w, residual, norm_w, eps=EPS):
+    y = (x.float() @ w.float().t()).to(x.dtype)
+    if norm_w is None:
+        return y, None
+    s = y.float() + residual.float()
+    r = s.to(x.dtype)
+    out = (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float()).to(x.dtype)
+    return out, r
+
+
+def ulp(ref: torch.Tensor) -> torch.Tensor:
+    """One unit in the last place of each reference value in its own dtype."""
+    mant = {torch.bfloat16: 7, torch.float16: 10, torch.float32: 23}[ref.dtype]
+    r = ref.float().abs().clamp_min(torch.finfo(torch.float32).tiny)
+    return torch.exp2(torch.floor(torch.log2(r)) - mant)
+
+
+def within(a, ref, tol=2e-2):
+    """Elementwise |a - ref| <= max(tol * RMS(ref), 1 ulp of ref).
+
+    The north-star bar is max |diff| <= 2e-2 * RMS(ref). A single rounding
+    flip of a bf16 output of magnitude >= 4 is 2^-5 = 0.031 > 0.02 * RMS when
+    RMS ~ 1 (RMSNorm outputs), so the bar is applied with a one-ulp allowance;
+    test_reference_path_has_the_same_ulp_flips shows the reference's own
+    library path needs the same allowance against an f32 restatement.
+    """
+    rms = ref.float().pow(2).mean().sqrt().item()
+    d = (a.float() - ref.float()).abs()
+    bound = torch.maximum(torch.full_like(d, tol * rms), ulp(ref))
+    worst = (d / bound).max().item()
+    return worst <= 1.0, f"max|diff|={d.max().item():.4g} rms={rms:.4g} worst/bound={worst:.3g}"
+
+
+@pytest.fixture(scope="module")
+def comm1(pgb):
+    import importlib
+
+    dist = importlib.import_module("pico-sglang_b200.distributed")
+    c = dist.PGBCommunicator(0, 1, 64 << 20, dist.create_uid())
+    yield c
+    c.close()
+
+
+def make(T, H, K, dtype, dev, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(T, K, device=dev, generator=g).to(dtype)
+    w = (torch.randn(H, K, device=dev, generator=g) * 0.02).to(dtype)
+    r = torch.randn(T, H, device=dev, generator=g).to(dtype)
+    nw = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).to(dtype)
+    return x, w, r, nw
+
+
+SHAPES = [
+    (1, 4096, 4096),
+    (8, 4096, 12288),
+    (32, 4096, 512),
+    (64, 5120, 1024),
+    (128, 4096, 1536),
+    (256, 4096, 4096),
+    (3, 200, 136),
+    (1000, 4096, 512),
+    (2048, 4096, 4096),
+]
+
+
+@pytest.mark.parametrize("T,H,K", SHAPES)
+def test_row_fused_addnorm_tp1(pgb, comm1, cuda_device, T, H, K):
+    ops = pgb.ops
+    x, w, r, nw = make(T, H, K, torch.bfloat16, cuda_device, T * 7 + K)
+    ref_out, ref_r = torch_ref(x, w, r, nw)
+    r_mine = r.clone()
+    out = ops.row_gemm_allreduce_addnorm(comm1, x, w, r_mine, nw, EPS)
+    comm1.check_status()
+    ok, msg = within(out, ref_out)
+    assert ok, "out " + msg
+    ok, msg = within(r_mine, ref_r)
+    assert ok, "residual " + msg
+
+
+@pytest.mark.parametrize("T,H,K", [(1, 4096, 4096), (200, 4096, 1024), (1500, 1024, 512)])
+def test_row_fused_no_norm_tp1(pgb, comm1, cuda_device, T, H, K):
+    x, w, r, _ = make(T, H, K, torch.bfloat16, cuda_device, 5 + T)
+    ref, _ = torch_ref(x, w, None, None)
+    y = pgb.ops.row_gemm_allreduce_addnorm(comm1, x, w, None, None, EPS)
+    comm1.check_status()
+    ok, msg = within(y, ref)
+    assert ok, msg
+
+
+def test_row_fused_fp16(pgb, comm1, cuda_device):
+    x, w, r, nw = make(16, 2048, 1024, torch.float16, cuda_device, 99)
+    ref_out, ref_r = torch_ref(x, w, r, nw)
+    r2 = r.clone()
+    out = pgb.ops.row_gemm_allreduce_addnorm(comm1, x, w, r2, nw, EPS)
+    comm1.check_status()
+    assert within(out, ref_out)[0] and within(r2, ref_r)[0]
+
+
+def test_row_fused_matches_reference_library_path(pgb, comm1, cuda_device):
+    """F.linear (cuBLAS) + flashinfer.fused_add_rmsnorm, the reference's own calls."""
+    flashinfer = pytest.importorskip("flashinfer")
+    for T in (1, 32, 256):
+        x, w, r, nw = make(T, 4096, 4096, torch.bfloat16, cuda_device, 1000 + T)
+        y = torch.nn.functional.linear(x, w)
+        r_ref = r.clone()
+        flashinfer.fused_add_rmsnorm(y, r_ref, nw, EPS)
+        r_mine = r.clone()
+        out = pgb.ops.row_gemm_allreduce_addnorm(comm1, x, w, r_mine, nw, EPS)
+        comm1.check_status()
+        ok, msg = within(out, y)
+        assert ok, f"T={T} out {msg}"
+        ok, msg = within(r_mine, r_ref)
+        assert ok, f"T={T} residual {msg}"
+
+
+def test_reference_path_has_the_same_ulp_flips(cuda_device):
+    """cuBLAS F.linear + flashinfer.fused_add_rmsnorm vs the f32 restatement:
+    its max |diff| also exceeds 2e-2 * RMS by one-ulp flips, and stays within
+    the one-ulp allowance."""
+    flashinfer = pytest.importorskip("flashinfer")
+    g = torch.Generator(device=cuda_device).manual_seed(77)
+    x = torch.randn(256, 4096, device=cuda_device, generator=g).bfloat16()
+    w = (torch.randn(4096, 4096, device=cuda_device, generator=g) * 0.02).bfloat16()
+    r = torch.randn(256, 4096, device=cuda_device, generator=g).bfloat16()
+    nw = (1.0 + 0.1 * torch.randn(4096, device=cuda_device, generator=g)).bfloat16()
+    ref_out, _ = torch_ref(x, w, r, nw)
+    y = torch.nn.functional.linear(x, w)
+    flashinfer.fused_add_rmsnorm(y, r.clone(), nw, EPS)
+    ok, msg = within(y, ref_out)
+    assert ok, msg
+    rms = ref_out.float().pow(2).mean().sqrt().item()
+    raw = (y.float() - ref_out.float()).abs().max().item()
+    print(f"reference library path: max|diff|={raw:.4g} = {raw / rms:.3g} x RMS")
+
+
+def test_row_fused_repeatable(pgb, comm1, cuda_device):
+    x, w, r, nw = make(8, 4096, 4096, torch.bfloat16, cuda_device, 3)
+    outs = []
+    for _ in range(4):
+        rr = r.clone()
+        outs.append((pgb.ops.row_gemm_allreduce_addnorm(comm1, x, w, rr, nw, EPS), rr))
+    torch.cuda.synchronize()
+    for o, rr in outs[1:]:
+        assert torch.equal(o, outs[0][0]) and torch.equal(rr, outs[0][1])
+
+
+def test_row_fused_cuda_graph_replay(pgb, comm1, cuda_device):
+    """Captured like the decode graphs (engine/graph.py:135-136): epochs live on the device."""
+    x, w, r, nw = make(16, 4096, 2048, torch.bfloat16, cuda_device, 21)
+    ref_out, _ = torch_ref(x, w, r, nw)
+    rr = r.clone()
+    out = torch.empty_like(r)
+    pgb.ops.row_gemm_allreduce_addnorm(comm1, x, w, rr, nw, EPS, out=out)  # warm-up
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            pgb.ops.row_gemm_allreduce_addnorm(comm1, x, w, rr, nw, EPS, out=out)
+    for _ in range(3):
+        rr.copy_(r)
+        graph.replay()
+        torch.cuda.synchronize()
+        comm1.check_status()
+        ok, msg = within(out, ref_out)
+        assert ok, msg
+    del graph
+
+
+def test_standalone_norms(pgb, cuda_device):
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    for dtype in (torch.bfloat16, torch.float32):
+        x = torch.randn(33, 4096, device=cuda_device, generator=g).to(dtype)
+        r = torch.randn(33, 4096, device=cuda_device, generator=g).to(dtype)
+        wn = torch.rand(4096, device=cuda_device, generator=g).to(dtype)
+        s = x.float() + r.float()
+        ref_r = s.to(dtype)
+        ref = (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + EPS) * wn.float()).to(dtype)
+        xx, rr = x.clone(), r.clone()
+        pgb.ops.fused_add_rmsnorm(xx, rr, wn, EPS)
+        torch.cuda.synchronize()
+        tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+        assert within(xx, ref, tol)[0] and within(rr, ref_r, tol)[0]
+        o = pgb.ops.rmsnorm(x, wn, EPS)
+        ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + EPS) * wn.float()).to(dtype)
+        torch.cuda.synchronize()
+        assert within(o, ref, tol)[0]
