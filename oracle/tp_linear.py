@@ -39,12 +39,20 @@ def round_to(a, dtype: str) -> np.ndarray:
 # ---------------------------------------------------------------- linears --
 
 
-def linear(x, w, bias=None, dtype: str = "bf16") -> np.ndarray:
+def linear(x, w, bias=None, dtype: str = "bf16", accum: str = "f64") -> np.ndarray:
     """y = x . w^T (+ bias), rounded to dtype.
 
     LinearTPImpl.forward = F.linear(x, self.weight, self.bias)
-    (python/picosgl/layers/linear.py:23-27).
+    (python/picosgl/layers/linear.py:23-27). accum="f64" (the default, used
+    by the tests) accumulates exactly enough to round correctly; accum="f32"
+    uses BLAS sgemm like the reference's CPU path (torch f32 matmul) and is
+    what the CPU-baseline timing runs.
     """
+    if accum == "f32":
+        y = np.asarray(x, np.float32) @ np.asarray(w, np.float32).T
+        if bias is not None:
+            y = y + np.asarray(bias, np.float32)
+        return round_to(y, dtype)
     y = np.asarray(x, np.float64) @ np.asarray(w, np.float64).T
     if bias is not None:
         y = y + np.asarray(bias, np.float64)
@@ -159,7 +167,7 @@ def col_shard_partitioned(wq, wk, wv, num_kv_heads: int, rank: int, n: int) -> n
 
 
 def row_parallel_addnorm(x_full, w_full, residual, norm_w, eps: float, n: int,
-                         dtype: str = "bf16", bias=None):
+                         dtype: str = "bf16", bias=None, accum: str = "f64"):
     """The fused op the CUDA library implements, restated unfused.
 
     Per rank: p_r = dtype(x_r . W_r^T (+ bias)) (LinearRowParallel.forward,
@@ -172,7 +180,7 @@ def row_parallel_addnorm(x_full, w_full, residual, norm_w, eps: float, n: int,
     parts = []
     for r in range(n):
         w_r, x_r = row_shard(w_full, x_full, r, n)
-        parts.append(linear(x_r, w_r, bias, dtype))
+        parts.append(linear(x_r, w_r, bias, dtype, accum))
     y = parts[0] if n == 1 else all_reduce_sum(parts, dtype)
     if norm_w is None:
         return y, None, y
@@ -181,7 +189,7 @@ def row_parallel_addnorm(x_full, w_full, residual, norm_w, eps: float, n: int,
 
 
 def tp_layer_step(h, a, m, residual, wts: dict, eps: float, n: int, rank: int = 0,
-                  dtype: str = "bf16"):
+                  dtype: str = "bf16", accum: str = "f64"):
     """One pass of the linear path of a decoder layer at TP size n.
 
     The order of LlamaDecoderLayer.forward (python/picosgl/models/llama.py:77-86):
@@ -193,8 +201,8 @@ def tp_layer_step(h, a, m, residual, wts: dict, eps: float, n: int, rank: int = 
     wts holds full (unsharded) weights: qkv, o, gate_up, down, ln1, ln2.
     Returns dict of the outputs on `rank`.
     """
-    qkv = linear(h, col_shard_merged([wts["qkv"]], rank, n), None, dtype)
-    x1, r1, _ = row_parallel_addnorm(a, wts["o"], residual, wts["ln1"], eps, n, dtype)
-    gu = linear(x1, col_shard_merged([wts["gate_up"]], rank, n), None, dtype)
-    x2, r2, _ = row_parallel_addnorm(m, wts["down"], r1, wts["ln2"], eps, n, dtype)
+    qkv = linear(h, col_shard_merged([wts["qkv"]], rank, n), None, dtype, accum)
+    x1, r1, _ = row_parallel_addnorm(a, wts["o"], residual, wts["ln1"], eps, n, dtype, accum=accum)
+    gu = linear(x1, col_shard_merged([wts["gate_up"]], rank, n), None, dtype, accum)
+    x2, r2, _ = row_parallel_addnorm(m, wts["down"], r1, wts["ln2"], eps, n, dtype, accum=accum)
     return {"qkv": qkv, "x1": x1, "r1": r1, "gate_up": gu, "x2": x2, "r2": r2}

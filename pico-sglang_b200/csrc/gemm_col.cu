@@ -71,17 +71,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float v[32];
           epi_load_chunk<BN>(g, tc, tmem, acc, col, v);
           if constexpr (SWAP) {
-            // Lane = output feature n, columns = tokens.
+            // Lane = output feature n, columns = tokens: transpose through
+            // shared memory and store 16-byte pieces of token rows.
             const int n = tc.p * kTileP + row;
-            const int t0 = tc.q * BN + col;
-            if (n < g.N) {
-              const float b = bias != nullptr ? io_to_f32<IO>(bias[n]) : 0.f;
+            if (bias != nullptr && n < g.N) {
+              const float b = io_to_f32<IO>(bias[n]);
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int t = t0 + j;
-                if (t < g.T) y[static_cast<size_t>(t) * g.N + n] = f32_to_io<IO>(v[j] + b);
-              }
+              for (int j = 0; j < 32; ++j) v[j] += b;
             }
+            const int N = g.N;
+            swap_epilogue_store<IO>(c.epi, v, tc.q * BN + col, g.T, tc.p * kTileP, N,
+                                    [&](int t, int n0, uint4 piece) {
+                                      *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
+                                    });
           } else {
             // Lane = token t, columns = output features.
             const int t = tc.p * kTileP + row;
@@ -123,18 +125,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 namespace {
 
-template <int BN>
-constexpr int col_stages() {
-  // Fill ~224 KB of shared memory with stages of (16 KB A + BN*128 B).
-  return (224 * 1024) / (kTileP * kBlockK * 2 + BN * kBlockK * 2) > 12
-             ? 12
-             : (224 * 1024) / (kTileP * kBlockK * 2 + BN * kBlockK * 2);
-}
-
 template <typename IO, int BN, bool SWAP>
 int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
                const void* bias, void* y, int T, int N, int K, uint8_t* ws, cudaStream_t stream) {
-  constexpr int STAGES = col_stages<BN>();
+  constexpr int STAGES = gemm_stages<BN>();
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kBytes <= 232448, "shared memory budget");
   auto kern = col_gemm_kernel<IO, BN, SWAP, STAGES>;

@@ -77,10 +77,20 @@ struct GemmSmem {
   // Layout (from a 1024-byte aligned base): A ring, B ring, barriers.
   static constexpr int kOffA = 0;
   static constexpr int kOffB = STAGES * kABytes;
-  static constexpr int kOffBar = kOffB + STAGES * kBBytes;
+  static constexpr int kOffEpi = kOffB + STAGES * kBBytes;
+  static constexpr int kEpiBytes = 32 * kTileP * 2;  // 32 tokens x 128 features, 16-bit
+  static constexpr int kOffBar = kOffEpi + kEpiBytes;
   static constexpr int kBarBytes = 8 * (2 * STAGES + 5) + 64;
   static constexpr int kBytes = kOffBar + kBarBytes + 1024;  // + alignment slack
 };
+
+// Pipeline depth that fills the shared-memory budget for a tile width.
+template <int BN>
+constexpr int gemm_stages() {
+  constexpr int kBudget = 216 * 1024;  // leaves room for the epilogue tile and barriers
+  constexpr int kStage = kTileP * kBlockK * 2 + BN * kBlockK * 2;
+  return kBudget / kStage > 12 ? 12 : kBudget / kStage;
+}
 
 struct GemmCtl {
   uint64_t* full;       // [STAGES]
@@ -93,6 +103,7 @@ struct GemmCtl {
   int* flag;
   uint8_t* a;
   uint8_t* b;
+  uint16_t* epi;  // [32][128] staging tile of the swap-orientation epilogue
 };
 
 template <int BN, int STAGES>
@@ -103,6 +114,7 @@ __device__ __forceinline__ GemmCtl gemm_carve_smem(uint8_t* raw) {
   GemmCtl c;
   c.a = base + L::kOffA;
   c.b = base + L::kOffB;
+  c.epi = reinterpret_cast<uint16_t*>(base + L::kOffEpi);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::kOffBar);
   c.full = bars;
   c.empty = bars + STAGES;
@@ -276,6 +288,14 @@ __device__ __forceinline__ void unpack8(uint4 u, float* v) {
   }
 }
 
+// Split-K partial of (tile pq, split s): BN/4 column groups x 128 rows of
+// float4, so the 32 lanes of a warp (consecutive rows) store and load 512
+// contiguous bytes per instruction.
+template <int BN>
+__device__ __forceinline__ float4* splitk_slab(const GemmShape& g, int pq, int s) {
+  return reinterpret_cast<float4*>(g.ws) + (static_cast<size_t>(pq) * g.splits + s) * (BN / 4) * kTileP;
+}
+
 // Split-K combine. On entry every epilogue thread has waited for acc_full.
 // Writes this unit's partial, arrives on the tile counter and returns true
 // when this CTA is the last of the tile's splits (it then owns the epilogue
@@ -284,17 +304,17 @@ template <int BN>
 __device__ __forceinline__ bool splitk_publish(const GemmShape& g, const GemmCtl& c,
                                                const TileCoord& tc, uint32_t tmem, int acc) {
   const int row = epi_row();
-  float* mine = g.ws + ((static_cast<size_t>(tc.pq) * g.splits + tc.s) * kTileP + row) * BN;
+  float4* mine = splitk_slab<BN>(g, tc.pq, tc.s);
 #pragma unroll 1
   for (int col = 0; col < BN; col += 32) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, col), r);
     tmem_ld_wait();
-    float4* dst = reinterpret_cast<float4*>(mine + col);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                  __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+      __stcg(mine + (col / 4 + j) * kTileP + row,
+             make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                         __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
   }
   __threadfence();
   named_bar_sync(1, kEpiThreads);
@@ -334,16 +354,41 @@ __device__ __forceinline__ void epi_load_chunk(const GemmShape& g, const TileCoo
       for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
       continue;
     }
-    const float4* src = reinterpret_cast<const float4*>(
-        g.ws + ((static_cast<size_t>(tc.pq) * g.splits + s) * kTileP + row) * BN + col);
+    const float4* src = splitk_slab<BN>(g, tc.pq, s) + (col / 4) * kTileP + row;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float4 t = __ldcg(src + j);
+      const float4 t = __ldcg(src + j * kTileP);
       v[4 * j] += t.x;
       v[4 * j + 1] += t.y;
       v[4 * j + 2] += t.z;
       v[4 * j + 3] += t.w;
     }
+  }
+}
+
+// Swap orientation: this thread holds v[j] = out(feature p*128 + row,
+// token t0 + j), j < 32. Stage the 32 x 128 block through shared memory so
+// it leaves as 16-byte pieces of token rows. emit(t, n0, piece) receives
+// 8 consecutive features [n0, n0 + 8) of token t. All 128 epilogue threads
+// call this together.
+template <typename IO, typename Emit>
+__device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* v, int t0, int T,
+                                                    int n_base, int N, Emit&& emit) {
+  const int row = epi_row();
+  named_bar_sync(1, kEpiThreads);  // previous chunk fully read
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    IO h = f32_to_io<IO>(v[j]);
+    epi[j * kTileP + row] = *reinterpret_cast<uint16_t*>(&h);
+  }
+  named_bar_sync(1, kEpiThreads);
+  const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int idx = tid + k * kEpiThreads;  // 512 pieces: 32 tokens x 16 pieces
+    const int j = idx >> 4, piece = idx & 15;
+    const int t = t0 + j, n0 = n_base + piece * 8;
+    if (t < T && n0 < N) emit(t, n0, *reinterpret_cast<const uint4*>(epi + j * kTileP + piece * 8));
   }
 }
 

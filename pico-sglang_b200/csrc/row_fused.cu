@@ -57,6 +57,25 @@ __device__ __forceinline__ void row_store_partial(const RowArgs& a, uint32_t par
   }
 }
 
+// 8 consecutive features [n0, n0 + 8) of token t into the reducing rank(s).
+template <typename IO>
+__device__ __forceinline__ void row_store_piece(const RowArgs& a, uint32_t parity, int t, int n0,
+                                                uint4 piece) {
+  const int H = a.g.N;
+  const size_t src_off = static_cast<size_t>(a.cm.rank) * a.rs.rows_cap * H;
+  int d0 = 0, d1 = a.cm.world;
+  size_t row = static_cast<size_t>(t);
+  if (!a.rs.oneshot) {
+    d0 = t / a.rs.rows_per;
+    d1 = d0 + 1;
+    row = static_cast<size_t>(t - d0 * a.rs.rows_per);
+  }
+  for (int d = d0; d < d1; ++d) {
+    IO* base = reinterpret_cast<IO*>(a.cm.slots[d] + parity * a.cm.slot_parity_bytes);
+    *reinterpret_cast<uint4*>(base + src_off + row * H + n0) = piece;
+  }
+}
+
 template <typename IO>
 __device__ __forceinline__ void row_store_partial_vec32(const RowArgs& a, uint32_t parity, int t,
                                                         int n0, const float* v) {
@@ -149,15 +168,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           epi_load_chunk<BN>(g, tc, tmem, acc, col, v);
           if constexpr (SWAP) {
             const int n = tc.p * kTileP + row;
-            const int t0 = tc.q * BN + col;
-            if (n < g.N) {
-              const float b = bias != nullptr ? io_to_f32<IO>(bias[n]) : 0.f;
-#pragma unroll 4
-              for (int j = 0; j < 32; ++j) {
-                const int t = t0 + j;
-                if (t < g.T) row_store_partial<IO>(a, parity, t, n, f32_to_io<IO>(v[j] + b));
-              }
+            if (bias != nullptr && n < g.N) {
+              const float b = io_to_f32<IO>(bias[n]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += b;
             }
+            swap_epilogue_store<IO>(c.epi, v, tc.q * BN + col, g.T, tc.p * kTileP, g.N,
+                                    [&](int t, int n0, uint4 piece) {
+                                      row_store_piece<IO>(a, parity, t, n0, piece);
+                                    });
           } else {
             const int t = tc.p * kTileP + row;
             const int n0 = tc.q * BN + col;
@@ -215,16 +234,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 namespace {
 
-template <int BN>
-constexpr int row_stages() {
-  return (224 * 1024) / (kTileP * kBlockK * 2 + BN * kBlockK * 2) > 12
-             ? 12
-             : (224 * 1024) / (kTileP * kBlockK * 2 + BN * kBlockK * 2);
-}
-
 template <typename IO, int BN, bool SWAP>
 int launch_row(pgb_comm* c, RowArgs args, const void* x, const void* w, cudaStream_t stream) {
-  constexpr int STAGES = row_stages<BN>();
+  constexpr int STAGES = gemm_stages<BN>();
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kBytes + 256 <= 232448, "shared memory budget");
   auto kern = row_fused_kernel<IO, BN, SWAP, STAGES>;

@@ -156,8 +156,10 @@ class LinearRowParallel(LinearTPImpl):
         if norm is not None and res is not None and res.shape == (T, N) and res.dtype == x2.dtype:
             out = ops.row_gemm_allreduce_addnorm(self._comm(), x2, self.weight, res, norm.weight, norm.eps,
                                                  bias=self.bias)
-            _CTX.fused = (out, norm, res)
-            return out.view(*x.shape[:-1], N)
+            if x.dim() != 2:
+                out = out.view(*x.shape[:-1], N)
+            _CTX.fused = (out, norm, res)  # the exact object handed to the consumer
+            return out
         if self._tp_size == 1:
             y = ops.col_gemm(x2, self.weight, self.bias)
         else:

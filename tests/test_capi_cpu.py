@@ -1,0 +1,79 @@
+"""The C-ABI library on the CPU: it loads, exports what include/pgb.h
+declares, and rejects bad arguments with a status + message (no GPU calls)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def header_symbols() -> set[str]:
+    text = (ROOT / "include" / "pgb.h").read_text()
+    return set(re.findall(r"PGB_API\s+[\w\s\*]+?\b(pgb_\w+)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol(pgb):
+    lib = pgb._lib.load()
+    declared = header_symbols()
+    assert len(declared) >= 18
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/pgb.h but not exported"
+    # The ctypes signature table covers exactly the header.
+    assert set(pgb._lib.declared_symbols()) == declared
+
+
+def test_version_and_uid(pgb):
+    lib = pgb._lib.load()
+    assert lib.pgb_version() == 100
+    a = (ctypes.c_uint8 * 128)()
+    b = (ctypes.c_uint8 * 128)()
+    assert lib.pgb_create_uid(a) == 0 and lib.pgb_create_uid(b) == 0
+    assert bytes(a) != bytes(b)
+
+
+def _last_error(lib) -> str:
+    return lib.pgb_last_error().decode()
+
+
+@pytest.mark.parametrize("rank,world", [(0, 0), (2, 2), (-1, 4), (0, 9)])
+def test_comm_create_rejects_bad_ranks(pgb, rank, world):
+    lib = pgb._lib.load()
+    uid = (ctypes.c_uint8 * 128)()
+    out = ctypes.c_void_p()
+    rc = lib.pgb_comm_create(rank, world, 1 << 20, uid, 0, ctypes.byref(out))
+    assert rc == pgb._lib.PGB_ERR_INVALID
+    assert "comm_create" in _last_error(lib)
+    assert out.value is None
+
+
+def test_gemm_rejects_bad_arguments_before_touching_the_device(pgb):
+    lib = pgb._lib.load()
+    rc = lib.pgb_col_gemm(1, 1, None, 1, 4, 16, 12, pgb._lib.PGB_BF16, 1, 1 << 20, None)
+    assert rc == pgb._lib.PGB_ERR_INVALID and "multiples of 8" in _last_error(lib)
+    rc = lib.pgb_col_gemm(1, 1, None, 1, 4, 16, 16, pgb._lib.PGB_F32, 1, 1 << 20, None)
+    assert rc == pgb._lib.PGB_ERR_UNSUPPORTED
+    rc = lib.pgb_col_gemm(1, 1, None, 1, -1, 16, 16, pgb._lib.PGB_BF16, 1, 1 << 20, None)
+    assert rc == pgb._lib.PGB_ERR_INVALID
+    rc = lib.pgb_row_gemm_allreduce_addnorm(None, 1, 1, None, 1, 1, 1e-6, 1, 4, 16, 16, 1, None)
+    assert rc == pgb._lib.PGB_ERR_INVALID and "null communicator" in _last_error(lib)
+    rc = lib.pgb_fused_add_rmsnorm(16, 16, 16, 1e-6, 4, 12, pgb._lib.PGB_BF16, None)
+    assert rc == pgb._lib.PGB_ERR_INVALID
+    rc = lib.pgb_all_reduce(None, 1, 4, pgb._lib.PGB_BF16, 0, None)
+    assert rc == pgb._lib.PGB_ERR_INVALID
+
+
+def test_errors_surface_as_python_exceptions(pgb):
+    with pytest.raises(pgb.PGBError, match="null communicator"):
+        pgb._lib.call("pgb_row_gemm_allreduce_addnorm", None, 1, 1, None, 1, 1, 1e-6, 1, 4, 16, 16, 1, None)
+
+
+def test_workspace_size_is_deterministic(pgb):
+    lib = pgb._lib.load()
+    a = lib.pgb_col_gemm_workspace_size(8, 6144, 4096)
+    assert a == lib.pgb_col_gemm_workspace_size(8, 6144, 4096) and a >= 256
+    assert lib.pgb_col_gemm_workspace_size(0, 1, 1) == 256

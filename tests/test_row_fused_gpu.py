@@ -38,18 +38,20 @@ def ulp(ref: torch.Tensor) -> torch.Tensor:
     return torch.exp2(torch.floor(torch.log2(r)) - mant)
 
 
-def within(a, ref, tol=2e-2):
-    """Elementwise |a - ref| <= max(tol * RMS(ref), 1 ulp of ref).
+def within(a, ref, tol=2e-2, ulps=2):
+    """Elementwise |a - ref| <= max(tol * RMS(ref), ulps * ulp(ref)).
 
     The north-star bar is max |diff| <= 2e-2 * RMS(ref). A single rounding
     flip of a bf16 output of magnitude >= 4 is 2^-5 = 0.031 > 0.02 * RMS when
-    RMS ~ 1 (RMSNorm outputs), so the bar is applied with a one-ulp allowance;
+    RMS ~ 1 (RMSNorm outputs), and the reference path rounds twice before the
+    residual and the output (the GEMM output, then the sum), so the bar is
+    applied with a two-ulp allowance (one ulp for a plain GEMM output);
     test_reference_path_has_the_same_ulp_flips shows the reference's own
-    library path needs the same allowance against an f32 restatement.
+    library path needs the allowance against an f32 restatement.
     """
     rms = ref.float().pow(2).mean().sqrt().item()
     d = (a.float() - ref.float()).abs()
-    bound = torch.maximum(torch.full_like(d, tol * rms), ulp(ref))
+    bound = torch.maximum(torch.full_like(d, tol * rms), ulps * ulp(ref))
     worst = (d / bound).max().item()
     return worst <= 1.0, f"max|diff|={d.max().item():.4g} rms={rms:.4g} worst/bound={worst:.3g}"
 
@@ -106,7 +108,7 @@ def test_row_fused_no_norm_tp1(pgb, comm1, cuda_device, T, H, K):
     ref, _ = torch_ref(x, w, None, None)
     y = pgb.ops.row_gemm_allreduce_addnorm(comm1, x, w, None, None, EPS)
     comm1.check_status()
-    ok, msg = within(y, ref)
+    ok, msg = within(y, ref, ulps=1)
     assert ok, msg
 
 
