@@ -161,6 +161,14 @@ PGB_API int pgb_fused_add_rmsnorm(void* x, void* residual, const void* w, float 
 PGB_API int pgb_rmsnorm(const void* x, const void* w, float eps, void* out, int T, int H, int dtype,
                 void* stream);
 
+/* ----------------------------------------------------------- diagnostics --
+ * Replay on the host the work decomposition a GEMM of this shape would use
+ * on `sms` SMs (all_streamk != 0: the row-parallel kernel's plan) with
+ * launch_grid CTAs (0: the planned grid), and check that it covers every
+ * tile and k-block exactly once with consistent contributor bookkeeping.
+ * Needs no GPU. Internal consistency check, no reference counterpart. */
+PGB_API int pgb_check_work_plan(int T, int N, int K, int sms, int all_streamk, int launch_grid);
+
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,7 @@ struct LocalLayout {
   static constexpr size_t kStatus = 0;      // int
   static constexpr size_t kEpoch = 64;      // uint32
   static constexpr size_t kArrive = 128;    // uint32[kNumBars]
+  static constexpr size_t kGridBar = 256;   // uint32 arrive at +0, generation at +64
   static constexpr size_t kCounters = 4096; // split-K tile counters
   static constexpr size_t kPartials = kCounters + kTileCounterBytes;
   static constexpr size_t kBytes = kPartials + kSplitScratchBytes;

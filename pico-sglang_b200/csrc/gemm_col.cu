@@ -20,6 +20,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
+    trace(1000);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&c.full[i], 1);
       mbar_init(&c.empty[i], 1);
@@ -55,21 +56,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row = epi_row();
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int unit = blockIdx.x; unit < g.num_units; unit += gridDim.x) {
-      const TileCoord tc = decode_unit(g, unit);
+    int n_units = 0;
+    (void)n_units;
+    SegIter it(g);
+    Seg tc;
+    while (it.next(g, tc)) {
       if (!mbar_wait(&c.acc_full[acc], acc_phase, g.wait_ns, c.abort)) {
         record_error(g.status, kDevTimeoutPipeline);
         *reinterpret_cast<volatile int*>(c.abort) = 1;
         break;
       }
       tc_fence_after();
-      bool owner = true;
-      if (g.splits > 1) owner = splitk_publish<BN>(g, c, tc, tmem, acc);
-      if (owner) {
+      if (threadIdx.x == 64) trace(400 + (n_units < 32 ? n_units : 31));
+      if (tc.nctb > 1) {
+        // Shared tile: leave an f32 partial for the reduction phase.
+        partial_store_tm<BN>(g, tc, tmem, acc);
+      } else {
 #pragma unroll 1
         for (int col = 0; col < BN; col += 32) {
           float v[32];
-          epi_load_chunk<BN>(g, tc, tmem, acc, col, v);
+          epi_load_chunk<BN>(tmem, acc, col, v);
           if constexpr (SWAP) {
             // Lane = output feature n, columns = tokens: transpose through
             // shared memory and store 16-byte pieces of token rows.
@@ -107,6 +113,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       tc_fence_before();
+      if (threadIdx.x == 64) trace(432 + (n_units < 32 ? n_units : 31));
+      ++n_units;
       mbar_arrive(&c.acc_empty[acc]);
       if (++acc == 2) {
         acc = 0;
@@ -121,6 +129,68 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(*c.tmem_base, 2 * BN);
   }
+  if (g.sk_first < g.tiles) {
+    // Reduction phase: the grid finishes the shared stream-K tiles, summing
+    // the contributors' partials in order. Each thread owns 4 features of a
+    // (tile, token) row per step and keeps 4 steps of loads in flight.
+    uint32_t* bar = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(g.status) + 64);
+    if (grid_barrier_local(bar, bar + 16, g.status, g.wait_ns)) {
+      const long long rows = static_cast<long long>(g.tiles - g.sk_first) * g.T;
+      const long long n4 = rows * 32;
+      const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
+      for (long long base = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; base < n4;
+           base += 4 * nthr) {
+        float4 a[4];
+        int tiles_[4], ts[4], f4[4], nc[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const long long i = base + k * nthr;
+          a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+          nc[k] = 0;
+          if (i >= n4) continue;
+          const long long rr = i >> 5;
+          tiles_[k] = g.sk_first + static_cast<int>(rr / g.T);
+          ts[k] = static_cast<int>(rr % g.T);
+          f4[k] = static_cast<int>(i & 31);
+          nc[k] = tile_contributors(g, tiles_[k]);
+        }
+        // Contributor-ordered sums; the loads of the 4 steps are independent.
+        for (int j = 0; j < g.max_contrib; ++j) {
+          bool any = false;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (j < nc[k]) {
+              any = true;
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                                          partial_tm<BN>(g, tiles_[k], j) + static_cast<size_t>(ts[k]) * kTileP) +
+                                      f4[k]);
+              a[k].x += v.x;
+              a[k].y += v.y;
+              a[k].z += v.z;
+              a[k].w += v.w;
+            }
+          }
+          if (!any) break;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (nc[k] < 2) continue;  // whole tiles were stored by their owner
+          const int n0 = (tiles_[k] % g.p_tiles) * kTileP + f4[k] * 4;
+          if (n0 >= g.N) continue;
+          if (bias != nullptr) {
+            a[k].x += io_to_f32<IO>(bias[n0]);
+            a[k].y += io_to_f32<IO>(bias[n0 + 1]);
+            a[k].z += io_to_f32<IO>(bias[n0 + 2]);
+            a[k].w += io_to_f32<IO>(bias[n0 + 3]);
+          }
+          IO h[4] = {f32_to_io<IO>(a[k].x), f32_to_io<IO>(a[k].y), f32_to_io<IO>(a[k].z),
+                     f32_to_io<IO>(a[k].w)};
+          *reinterpret_cast<uint2*>(y + static_cast<size_t>(ts[k]) * g.N + n0) = *reinterpret_cast<uint2*>(h);
+        }
+      }
+    }
+  }
+  if (threadIdx.x == 0) trace(1001);
 }
 
 namespace {
@@ -151,19 +221,31 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
   g.N = N;
   g.K = K;
   g.kblocks = p.kblocks;
-  g.splits = p.splits;
   g.p_tiles = p.p_tiles;
   g.q_tiles = p.q_tiles;
-  g.num_units = p.units;
+  g.tiles = p.tiles;
+  g.dp_rounds = p.dp_rounds;
+  g.sk_first = p.sk_first;
+  g.grid = p.grid;
+  g.sk_grid = p.sk_grid;
+  g.max_contrib = p.max_contrib;
   g.status = reinterpret_cast<int*>(ws);
-  g.tile_counters = reinterpret_cast<uint32_t*>(ws + kWsHeaderBytes);
-  g.ws = reinterpret_cast<float*>(ws + kWsHeaderBytes + p.counter_bytes);
+  g.ws = reinterpret_cast<float*>(ws + kWsHeaderBytes);
   g.wait_ns = 2000000000ull;  // 2 s: far beyond any legitimate pipeline stall
 
-  kern<<<p.grid, kGemmThreads, L::kBytes, stream>>>(SWAP ? tm_w : tm_x, SWAP ? tm_x : tm_w, g,
-                                                    static_cast<IO*>(y),
-                                                    static_cast<const IO*>(bias));
-  PGB_CUDA_TRY(cudaGetLastError());
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // the reduction phase waits on every CTA
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const CUtensorMap& ta = SWAP ? tm_w : tm_x;
+  const CUtensorMap& tb = SWAP ? tm_x : tm_w;
+  PGB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, g, static_cast<IO*>(y), static_cast<const IO*>(bias)));
   return PGB_OK;
 }
 
@@ -225,3 +307,11 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
   if (dtype == PGB_BF16) return dispatch_col<__nv_bfloat16>(p, dev, x, w, bias, y, T, N, K, ws, s);
   return dispatch_col<__half>(p, dev, x, w, bias, y, T, N, K, ws, s);
 }
+
+#ifdef PGB_TRACE
+// Work-build only: point this translation unit's trace buffer at `buf`.
+extern "C" PGB_API int pgb_debug_set_trace(void* buf) {
+  cudaError_t e = cudaMemcpyToSymbol(pgb::pgb_trace_buf, &buf, sizeof(buf));
+  return e == cudaSuccess ? 0 : 2;
+}
+#endif

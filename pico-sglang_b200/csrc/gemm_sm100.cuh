@@ -22,11 +22,9 @@
 //                  128-row MMA side is always filled by weight rows and the
 //                  token side is only as wide as the batch.
 //
-// Split-K. A (P, Q) tile may be cut into `splits` K ranges handled by
-// different CTAs. Each writes its f32 partial into scratch, and the last CTA
-// to arrive on the tile's counter adds the others' partials to its own TMEM
-// accumulator and runs the epilogue. Counters are reset by that CTA, so the
-// scratch needs zeroing only once, when it is created.
+// Shared tiles (stream-K, see GemmShape): a CTA that covers only part of a
+// tile's K range stores its f32 partial; after a grid barrier all warps sum
+// the partials of every shared tile in contributor order.
 #pragma once
 
 #include "sm100.cuh"
@@ -40,33 +38,106 @@ constexpr int kEpiThreads = 128;     // warps 2..5
 constexpr int kMaxRanks = 8;
 
 // Everything the GEMM loop needs to know about the problem.
+//
+// Work decomposition. The output is cut into tiles of 128 (P) x BN (Q); a
+// tile's reduction dimension is `kblocks` k-blocks of 64. Tiles
+// [0, sk_first) are whole tiles dealt round-robin: CTA c computes tiles
+// c, c + grid, ... (dp_rounds of them at most). Tiles [sk_first, tiles) are
+// stream-K tiles: their k-blocks are laid end to end and CTA c takes the
+// contiguous range [c*total/grid, (c+1)*total/grid) of them, cut at tile
+// boundaries into segments. With sk_first = dp_rounds * grid every CTA
+// streams the same number of k-blocks (+-1), so no SM idles while others
+// finish a last partial wave. A stream-K tile shared by several CTAs is
+// finished after a grid barrier (cooperative launch) by all warps together,
+// adding the contributors' f32 partials in contributor order, so the result
+// does not depend on timing.
 struct GemmShape {
   int T, N, K;
-  int kblocks;   // ceil(K / 64)
-  int splits;    // K splits per (P, Q) tile, 1 <= splits <= kblocks
-  int p_tiles;   // tiles along the MMA M side
-  int q_tiles;   // tiles along the MMA N side
-  int num_units; // p_tiles * q_tiles * splits
-  float* ws;                 // split-K partials [p_tiles*q_tiles][splits][128][BN] f32
-  uint32_t* tile_counters;   // [p_tiles*q_tiles], zero at rest
-  int* status;               // device status word (first error wins)
-  uint64_t wait_ns;          // budget for every intra-kernel wait
+  int kblocks;      // ceil(K / 64)
+  int p_tiles;      // tiles along the MMA M side
+  int q_tiles;      // tiles along the MMA N side
+  int tiles;        // p_tiles * q_tiles
+  int dp_rounds;    // whole tiles per CTA before the stream-K part
+  int sk_first;     // first stream-K tile (== tiles: no stream-K part)
+  int grid;         // CTAs taking part in the round-robin part (<= gridDim.x)
+  int sk_grid;      // CTAs taking part in the stream-K part, <= grid and <=
+                    // its k-block count, so every stream-K range is non-empty
+  int max_contrib;  // partial slabs reserved per stream-K tile
+  float* ws;        // partials [tiles - sk_first][max_contrib][BN tokens][128 features] f32
+  int* status;      // device status word (first error wins); the grid
+                    // barrier's counters follow it at +64 and +128 bytes
+  uint64_t wait_ns; // budget for every intra-kernel wait
 };
 
-struct TileCoord {
-  int p, q, s, pq, kb0, kb1;
+// One contiguous piece of a tile's reduction handled by this CTA.
+struct Seg {
+  int tile, p, q;
+  int kb0, kb1;   // k-block range [kb0, kb1)
+  int contrib;    // index of this CTA among the tile's contributors
+  int nctb;       // number of contributors (1 = this CTA owns the whole tile)
 };
 
-__device__ __forceinline__ TileCoord decode_unit(const GemmShape& g, int unit) {
-  TileCoord c;
-  c.s = unit % g.splits;
-  c.pq = unit / g.splits;
-  c.p = c.pq % g.p_tiles;
-  c.q = c.pq / g.p_tiles;
-  c.kb0 = static_cast<int>((static_cast<long long>(c.s) * g.kblocks) / g.splits);
-  c.kb1 = static_cast<int>((static_cast<long long>(c.s + 1) * g.kblocks) / g.splits);
-  return c;
+// CTA whose stream-K range contains stream-K k-block u.
+__host__ __device__ __forceinline__ int streamk_cta_of(long long u, long long total, int grid) {
+  return static_cast<int>(((u + 1) * grid - 1) / total);
 }
+
+__host__ __device__ __forceinline__ long long streamk_total(const GemmShape& g) {
+  return static_cast<long long>(g.tiles - g.sk_first) * g.kblocks;
+}
+
+// Iterates the segments of CTA `cta` in order: its whole tiles, then its
+// stream-K range. All roles of a CTA walk the same sequence. Host-callable
+// so the decomposition can be checked without a GPU.
+struct SegIter {
+  long long u, u1, total;
+  int t, round, cta;
+  __host__ __device__ __forceinline__ SegIter(const GemmShape& g, int cta_) {
+    cta = cta_;
+    total = streamk_total(g);
+    round = 0;
+    t = cta;
+    if (cta < g.sk_grid && total > 0) {
+      u = total * cta / g.sk_grid;
+      u1 = total * (cta + 1) / g.sk_grid;
+    } else {  // no stream-K part, or a CTA beyond the stream-K grid
+      u = u1 = 0;
+    }
+    if (cta >= g.grid) round = g.dp_rounds;
+  }
+  __device__ __forceinline__ explicit SegIter(const GemmShape& g) : SegIter(g, static_cast<int>(blockIdx.x)) {}
+  __host__ __device__ __forceinline__ bool next(const GemmShape& g, Seg& s) {
+    if (round < g.dp_rounds) {
+      s.tile = t + round * g.grid;
+      ++round;
+      if (s.tile < g.sk_first) {
+        s.kb0 = 0;
+        s.kb1 = g.kblocks;
+        s.contrib = 0;
+        s.nctb = 1;
+        s.p = s.tile % g.p_tiles;
+        s.q = s.tile / g.p_tiles;
+        return true;
+      }
+      round = g.dp_rounds;  // ragged last round: no more whole tiles
+    }
+    if (u >= u1) return false;
+    const int rel = static_cast<int>(u / g.kblocks);
+    s.tile = g.sk_first + rel;
+    s.kb0 = static_cast<int>(u - static_cast<long long>(rel) * g.kblocks);
+    const long long rem = u1 - u;
+    s.kb1 = rem < static_cast<long long>(g.kblocks - s.kb0) ? s.kb0 + static_cast<int>(rem) : g.kblocks;
+    u += s.kb1 - s.kb0;
+    const long long first = static_cast<long long>(rel) * g.kblocks;
+    const int c0 = streamk_cta_of(first, total, g.sk_grid);
+    const int c1 = streamk_cta_of(first + g.kblocks - 1, total, g.sk_grid);
+    s.contrib = cta - c0;
+    s.nctb = c1 - c0 + 1;
+    s.p = s.tile % g.p_tiles;
+    s.q = s.tile / g.p_tiles;
+    return true;
+  }
+};
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -139,13 +210,17 @@ __device__ __forceinline__ void gemm_producer(const GemmShape& g, const GemmCtl&
 #pragma unroll
   for (int i = 0; i < STAGES; ++i) issued[i] = -1;
   bool ok = true;
-  for (int unit = blockIdx.x; unit < g.num_units && ok; unit += gridDim.x) {
-    const TileCoord tc = decode_unit(g, unit);
+  int n_issued = 0;
+  SegIter it(g);
+  Seg tc;
+  while (ok && it.next(g, tc)) {
     for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
       if (!mbar_wait(&c.empty[stage], phase ^ 1u, g.wait_ns, c.abort)) {
         ok = false;
         break;
       }
+      trace(n_issued < 200 ? n_issued : 1023);
+      ++n_issued;
       mbar_arrive_expect_tx(&c.full[stage], L::kStageBytes);
       tma_load_2d(tm_a, &c.full[stage], c.a + stage * L::kABytes, kb * kBlockK, tc.p * kTileP,
                   hint_a);
@@ -178,8 +253,10 @@ __device__ __forceinline__ void gemm_mma(const GemmShape& g, const GemmCtl& c, u
   const uint32_t tmem = *c.tmem_base;
   bool ok = true;
   bool any_commit = false;
-  for (int unit = blockIdx.x; unit < g.num_units && ok; unit += gridDim.x) {
-    const TileCoord tc = decode_unit(g, unit);
+  int n_full = 0;
+  SegIter it(g);
+  Seg tc;
+  while (ok && it.next(g, tc)) {
     if (!mbar_wait(&c.acc_empty[acc], acc_phase ^ 1u, g.wait_ns, c.abort)) {
       ok = false;
       break;
@@ -191,6 +268,8 @@ __device__ __forceinline__ void gemm_mma(const GemmShape& g, const GemmCtl& c, u
         ok = false;
         break;
       }
+      trace(n_full < 200 ? 200 + n_full : 1023);
+      ++n_full;
       tc_fence_after();
       const uint64_t da = umma_desc_sw128_kmajor(smem_u32(c.a + stage * L::kABytes));
       const uint64_t db = umma_desc_sw128_kmajor(smem_u32(c.b + stage * L::kBBytes));
@@ -288,82 +367,94 @@ __device__ __forceinline__ void unpack8(uint4 u, float* v) {
   }
 }
 
-// Split-K partial of (tile pq, split s): BN/4 column groups x 128 rows of
-// float4, so the 32 lanes of a warp (consecutive rows) store and load 512
-// contiguous bytes per instruction.
+// Load 32 accumulator columns [col, col + 32) of accumulator acc.
 template <int BN>
-__device__ __forceinline__ float4* splitk_slab(const GemmShape& g, int pq, int s) {
-  return reinterpret_cast<float4*>(g.ws) + (static_cast<size_t>(pq) * g.splits + s) * (BN / 4) * kTileP;
+__device__ __forceinline__ void epi_load_chunk(uint32_t tmem, int acc, int col, float* v) {
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, col), r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// Split-K combine. On entry every epilogue thread has waited for acc_full.
-// Writes this unit's partial, arrives on the tile counter and returns true
-// when this CTA is the last of the tile's splits (it then owns the epilogue
-// and must add the other splits' partials, see splitk_add_others).
+// Number of CTAs contributing to `tile` (1 for whole tiles).
+__host__ __device__ __forceinline__ int tile_contributors(const GemmShape& g, int tile) {
+  if (tile < g.sk_first) return 1;
+  const long long total = streamk_total(g);
+  const long long first = static_cast<long long>(tile - g.sk_first) * g.kblocks;
+  return streamk_cta_of(first + g.kblocks - 1, total, g.sk_grid) - streamk_cta_of(first, total, g.sk_grid) + 1;
+}
+
+// Token-major f32 partial of stream-K tile `tile`, contributor j, in swap
+// orientation: [BN tokens][128 features]. A warp stores 128 contiguous bytes
+// per token, and the reduction phase reads 8 consecutive features of a token
+// as two float4.
 template <int BN>
-__device__ __forceinline__ bool splitk_publish(const GemmShape& g, const GemmCtl& c,
-                                               const TileCoord& tc, uint32_t tmem, int acc) {
+__device__ __forceinline__ float* partial_tm(const GemmShape& g, int tile, int j) {
+  return g.ws + (static_cast<size_t>(tile - g.sk_first) * g.max_contrib + j) * BN * kTileP;
+}
+
+// Store this segment's accumulator (acc) as a token-major f32 partial.
+// Called by the 128 epilogue threads; tokens >= T are skipped.
+template <int BN>
+__device__ __forceinline__ void partial_store_tm(const GemmShape& g, const Seg& sg, uint32_t tmem,
+                                                 int acc) {
   const int row = epi_row();
-  float4* mine = splitk_slab<BN>(g, tc.pq, tc.s);
+  if (sg.contrib < 0 || sg.contrib >= g.max_contrib || sg.tile < g.sk_first) {
+    // Never store outside the reserved slabs; report instead.
+    if (row == 0) record_error(g.status, kDevBadArgs);
+    return;
+  }
+  float* dst = partial_tm<BN>(g, sg.tile, sg.contrib);
 #pragma unroll 1
   for (int col = 0; col < BN; col += 32) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, col), r);
     tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      __stcg(mine + (col / 4 + j) * kTileP + row,
-             make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                         __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+    for (int j = 0; j < 32; ++j) {
+      const int t = sg.q * BN + col + j;
+      if (t < g.T) __stcg(dst + static_cast<size_t>(col + j) * kTileP + row, __uint_as_float(r[j]));
+    }
   }
-  __threadfence();
-  named_bar_sync(1, kEpiThreads);
-  if (threadIdx.x == 64) {
-    const uint32_t old = atom_add_acqrel_gpu(&g.tile_counters[tc.pq], 1u);
-    const bool last = (old == static_cast<uint32_t>(g.splits - 1));
-    if (last) g.tile_counters[tc.pq] = 0u;
-    *c.flag = last ? 1 : 0;
-  }
-  named_bar_sync(1, kEpiThreads);
-  const bool last = (*reinterpret_cast<volatile int*>(c.flag) != 0);
-  if (last) __threadfence();
-  named_bar_sync(1, kEpiThreads);  // flag may be rewritten by the next tile
-  return last;
 }
 
-// Load 32 accumulator columns starting at col and, for split-K, add the
-// partials of all splits in split order (the CTA's own partial taken from
-// TMEM), so the result does not depend on which split finished last.
-template <int BN>
-__device__ __forceinline__ void epi_load_chunk(const GemmShape& g, const TileCoord& tc,
-                                               uint32_t tmem, int acc, int col, float* v) {
-  uint32_t r[32];
-  tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, col), r);
-  tmem_ld_wait();
-  if (g.splits == 1) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    return;
-  }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = 0.f;
-  const int row = epi_row();
-  for (int s = 0; s < g.splits; ++s) {
-    if (s == tc.s) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]);
-      continue;
+// Grid-wide barrier for a cooperative launch on one GPU. arrive/gen live in
+// global memory and are zero at rest; the last CTA to arrive resets the
+// counter and bumps the generation. Bounded: returns false (and records an
+// error) when the wait runs out or another CTA already failed.
+__device__ __forceinline__ bool grid_barrier_local(uint32_t* arrive, uint32_t* gen, int* status,
+                                                   uint64_t wait_ns) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint32_t g0 = ld_acquire_gpu(gen);
+    __threadfence();
+    const uint32_t old = atom_add_acqrel_gpu(arrive, 1u);
+    if (old == gridDim.x - 1) {
+      *arrive = 0u;
+      __threadfence();
+      st_release_gpu(gen, g0 + 1u);
+    } else {
+      Deadline d(wait_ns);
+      volatile int* st = status;
+      while (ld_acquire_gpu(gen) == g0) {
+        if (d.expired()) {
+          record_error(status, kDevTimeoutGrid);
+          ok = 0;
+          break;
+        }
+        if ((d.n & 255u) == 0u && *st != 0) {
+          ok = 0;
+          break;
+        }
+      }
     }
-    const float4* src = splitk_slab<BN>(g, tc.pq, s) + (col / 4) * kTileP + row;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float4 t = __ldcg(src + j * kTileP);
-      v[4 * j] += t.x;
-      v[4 * j + 1] += t.y;
-      v[4 * j + 2] += t.z;
-      v[4 * j + 3] += t.w;
-    }
+    s_ok = ok;
   }
+  __syncthreads();
+  return s_ok != 0;
 }
 
 // Swap orientation: this thread holds v[j] = out(feature p*128 + row,

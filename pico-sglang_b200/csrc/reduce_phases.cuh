@@ -185,33 +185,25 @@ __device__ __forceinline__ float block_sum(float v, float* red /* >= 32 floats *
   return t;
 }
 
-// Phase 2 for one row: sum the world partials of row t, then either write
-// the sum (do_norm == 0) or residual-add + RMSNorm it. Writes out[t] and
+// Phase 2 for one row t: obtain the f32 sum of row t's sources for every
+// 8-feature vector from sum8(t, n0, float[8]), round it to the I/O type (the
+// reference materialises the reduced tensor in that type), then either write
+// it (do_norm == 0) or residual-add + RMSNorm it. Writes out[t] and
 // residual[t] locally and, for two-shot, pushes both rows to every peer's
 // result region. MAXV bounds the 8-element vectors per thread.
-template <typename IO, typename SlotT, int MAXV>
+template <typename IO, int MAXV, typename Sum8>
 __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity,
                                            int t, int width, IO* out, IO* residual,
-                                           const IO* norm_w, float eps, int do_norm,
-                                           float* red) {
+                                           const IO* norm_w, float eps, int do_norm, float* red,
+                                           Sum8&& sum8) {
   const int nvec = width >> 3;
-  const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
-  const SlotT* slot0 = reinterpret_cast<const SlotT*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes);
-  const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
   float s[MAXV][8];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
     if (v < nvec) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) s[i][j] = 0.f;
-      for (int src = 0; src < cm.world; ++src) {
-        float p[8];
-        load8<SlotT>(slot0 + src * src_stride + static_cast<size_t>(lr) * width + v * 8, p);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s[i][j] += p[j];
-      }
+      sum8(t, v * 8, s[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) s[i][j] = round_io<IO>(s[i][j]);
       if (do_norm) {
@@ -228,15 +220,6 @@ __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs
   float rcp = 1.f;
   if (do_norm) rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
   const bool push = !rs.oneshot && cm.world > 1;
-  IO* res_planes[PGB_MAX_RANKS];
-  IO* out_planes[PGB_MAX_RANKS];
-  if (push) {
-    for (int d = 0; d < cm.world; ++d) {
-      uint8_t* base = cm.results[d] + parity * cm.result_parity_bytes;
-      out_planes[d] = reinterpret_cast<IO*>(base);
-      res_planes[d] = reinterpret_cast<IO*>(base + cm.result_parity_bytes / 2);
-    }
-  }
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int v = threadIdx.x + i * blockDim.x;
@@ -257,13 +240,36 @@ __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs
       if (push) {
         for (int d = 0; d < cm.world; ++d) {
           if (d == cm.rank) continue;
-          store8<IO>(out_planes[d] + off, o);
-          if (do_norm) store8<IO>(res_planes[d] + off, s[i]);
+          uint8_t* base = cm.results[d] + parity * cm.result_parity_bytes;
+          store8<IO>(reinterpret_cast<IO*>(base) + off, o);
+          if (do_norm) store8<IO>(reinterpret_cast<IO*>(base + cm.result_parity_bytes / 2) + off, s[i]);
         }
       }
     }
   }
 }
+
+// Sum over the ranks' partial rows pushed into this rank's slot region.
+template <typename SlotT>
+struct SlotSum8 {
+  const CommDev& cm;
+  const RowSplit& rs;
+  uint32_t parity;
+  int width;
+  __device__ __forceinline__ void operator()(int t, int n0, float* out) const {
+    const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
+    const SlotT* slot0 = reinterpret_cast<const SlotT*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes);
+    const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[j] = 0.f;
+    for (int src = 0; src < cm.world; ++src) {
+      float p[8];
+      load8<SlotT>(slot0 + src * src_stride + static_cast<size_t>(lr) * width + n0, p);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] += p[j];
+    }
+  }
+};
 
 // Phase 3 (two-shot): copy the rows owned by other ranks from this rank's
 // result region into out / residual.

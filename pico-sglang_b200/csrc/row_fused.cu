@@ -38,6 +38,7 @@ struct RowArgs {
   const void* bias;
   float eps;
   int do_norm;
+  uint32_t* grid_bar;  // local grid barrier counters (arrive, generation at +64 B)
 };
 
 template <typename IO>
@@ -136,6 +137,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t e = s_epoch;
   const uint32_t parity = e & 1u;
+  // Decode plans put every tile in the stream-K part; their segments leave
+  // f32 partials that the reduction phases combine.
+  const bool staged = g.sk_first == 0 && g.tiles > 0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -149,23 +153,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tmem = *c.tmem_base;
     const int row = epi_row();
     const IO* bias = static_cast<const IO*>(a.bias);
+    (void)row;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int unit = blockIdx.x; unit < g.num_units; unit += gridDim.x) {
-      const TileCoord tc = decode_unit(g, unit);
+    SegIter it(g);
+    Seg tc;
+    while (it.next(g, tc)) {
       if (!mbar_wait(&c.acc_full[acc], acc_phase, g.wait_ns, c.abort)) {
         record_error(g.status, kDevTimeoutPipeline);
         *reinterpret_cast<volatile int*>(c.abort) = 1;
         break;
       }
       tc_fence_after();
-      bool owner = true;
-      if (g.splits > 1) owner = splitk_publish<BN>(g, c, tc, tmem, acc);
-      if (owner) {
+      if (staged) {
+        // Decode: every segment leaves an f32 token-major partial; the
+        // reduction phases below combine contributors, ranks and residual.
+        partial_store_tm<BN>(g, tc, tmem, acc);
+      } else {
+        // Whole tiles (prefill): round and store straight into the slots of
+        // the rank(s) that reduce these rows.
 #pragma unroll 1
         for (int col = 0; col < BN; col += 32) {
           float v[32];
-          epi_load_chunk<BN>(g, tc, tmem, acc, col, v);
+          epi_load_chunk<BN>(tmem, acc, col, v);
           if constexpr (SWAP) {
             const int n = tc.p * kTileP + row;
             if (bias != nullptr && n < g.N) {
@@ -213,21 +223,67 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 
   const bool multi = a.cm.world > 1;
-  // A pipeline timeout anywhere on this GPU poisons the status; the barrier
-  // then stops waiting and phase 2 is skipped.
-  const bool ok = grid_cross_barrier(a.cm, kBarPartials, e, multi);
   IO* out = static_cast<IO*>(a.out);
   IO* residual = static_cast<IO*>(a.residual);
   const IO* norm_w = static_cast<const IO*>(a.norm_w);
-  if (ok) {
+  const IO* bias = static_cast<const IO*>(a.bias);
+  // Sum of the contributors' f32 partials (plus the bias once) for
+  // features [n0, n0 + 8) of token t; swap orientation, so the tile is
+  // n0 / 128 and the partial row is token-major.
+  auto slab_sum8 = [&](int t, int n0, float* o) {
+    const int tile = n0 / kTileP;
+    const int n = tile_contributors(g, tile);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 0.f;
+    for (int j = 0; j < n; ++j) {
+      float p[8];
+      load8<float>(partial_tm<BN>(g, tile, j) + static_cast<size_t>(t) * kTileP + (n0 % kTileP), p);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] += p[q];
+    }
+    if (bias != nullptr) {
+      float b[8];
+      load8<IO>(bias + n0, b);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) o[q] += b[q];
+    }
+  };
+
+  bool ok = true;
+  if (staged && multi) {
+    // Phase 1.5: combine this rank's contributors, round to the I/O type and
+    // push each 8-feature piece to the rank(s) that reduce its row.
+    uint32_t* gb = a.grid_bar;
+    ok = grid_barrier_local(gb, gb + 16, g.status, g.wait_ns);
+    if (ok) {
+      const int nvec = g.N >> 3;
+      const long long items = static_cast<long long>(g.T) * nvec;
+      for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items;
+           i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int t = static_cast<int>(i / nvec), n0 = static_cast<int>(i % nvec) * 8;
+        float v[8];
+        slab_sum8(t, n0, v);
+        row_store_piece<IO>(a, parity, t, n0, pack8<IO>(v));
+      }
+    }
+  }
+  // A failure anywhere on this GPU poisons the status; the barriers then
+  // stop waiting and the later phases are skipped.
+  const bool ok0 = grid_cross_barrier(a.cm, kBarPartials, e, multi) && ok;
+  if (ok0) {
     const int r0 = a.rs.first(a.cm.rank), r1 = a.rs.last(a.cm.rank);
-    for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x)
-      reduce_row<IO, IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps,
-                                     a.do_norm, s_red);
+    for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x) {
+      if (staged && !multi)
+        reduce_row<IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps,
+                                   a.do_norm, s_red, slab_sum8);
+      else
+        reduce_row<IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps,
+                                   a.do_norm, s_red, SlotSum8<IO>{a.cm, a.rs, parity, g.N});
+    }
   }
   if (multi && !a.rs.oneshot) {
     const bool ok2 = grid_cross_barrier(a.cm, kBarResults, e, true);
-    if (ok && ok2) gather_rows<IO>(a.cm, a.rs, parity, g.N, out, residual, a.do_norm);
+    if (ok0 && ok2) gather_rows<IO>(a.cm, a.rs, parity, g.N, out, residual, a.do_norm);
   }
   comm_end(a.cm, e);
 }
@@ -349,22 +405,26 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
     return set_error(PGB_ERR_INVALID,
                      "row_gemm: %d x %d payload exceeds the communicator buffer (max_bytes=%zu)", T,
                      N, comm->max_bytes);
-  const GemmPlan p = plan_gemm(T, N, K_local, comm->sm_count, kSplitScratchBytes);
-  if (static_cast<size_t>(p.p_tiles) * p.q_tiles * 4u > kTileCounterBytes)
-    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: too many tiles (%d)", p.p_tiles * p.q_tiles);
+  const GemmPlan p = plan_gemm(T, N, K_local, comm->sm_count, kSplitScratchBytes, /*all_streamk=*/true);
+  if (p.counter_bytes > kTileCounterBytes)
+    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: too many tiles (%d)", p.tiles);
 
   RowArgs args{};
   args.g.T = T;
   args.g.N = N;
   args.g.K = K_local;
   args.g.kblocks = p.kblocks;
-  args.g.splits = p.splits;
   args.g.p_tiles = p.p_tiles;
   args.g.q_tiles = p.q_tiles;
-  args.g.num_units = p.units;
+  args.g.tiles = p.tiles;
+  args.g.dp_rounds = p.dp_rounds;
+  args.g.sk_first = p.sk_first;
+  args.g.grid = p.grid;
+  args.g.sk_grid = p.sk_grid;
+  args.g.max_contrib = p.max_contrib;
   args.g.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
-  args.g.tile_counters = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kCounters);
   args.g.ws = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
+  args.grid_bar = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kGridBar);
   args.g.wait_ns = 2000000000ull;
   args.cm = comm_dev(comm);
   args.rs = rs;

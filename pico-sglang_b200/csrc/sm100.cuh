@@ -245,4 +245,18 @@ __device__ __forceinline__ bool epoch_reached(uint32_t seen, uint32_t want) {
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
 
+// Optional pipeline timeline for performance investigation. Compiled only
+// with -DPGB_TRACE; the host sets pgb_trace_buf to a zeroed device buffer of
+// [gridDim.x][kTraceSlots] u64 (ns timestamps). Off in normal builds.
+#ifdef PGB_TRACE
+constexpr int kTraceSlots = 1024;
+__device__ uint64_t* pgb_trace_buf;
+__device__ __forceinline__ void trace(int slot) {
+  if (pgb_trace_buf != nullptr && slot < kTraceSlots)
+    pgb_trace_buf[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = globaltimer_ns();
+}
+#else
+__device__ __forceinline__ void trace(int) {}
+#endif
+
 }  // namespace pgb

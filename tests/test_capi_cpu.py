@@ -77,3 +77,25 @@ def test_workspace_size_is_deterministic(pgb):
     a = lib.pgb_col_gemm_workspace_size(8, 6144, 4096)
     assert a == lib.pgb_col_gemm_workspace_size(8, 6144, 4096) and a >= 256
     assert lib.pgb_col_gemm_workspace_size(0, 1, 1) == 256
+
+
+SHAPE_SWEEP = [
+    (T, N, K)
+    for T in (1, 3, 8, 32, 33, 64, 128, 200, 256, 257, 1000, 8192)
+    for N, K in ((6144, 4096), (24576, 4096), (4096, 512), (4096, 12288), (768, 4096), (3072, 4096),
+                 (200, 136), (128, 64), (5120, 25600), (10240, 5120))
+]
+
+
+@pytest.mark.parametrize("sms", [148, 132, 7])
+def test_work_decomposition_covers_every_k_block_once(pgb, sms):
+    """Every planned GEMM (column: round-robin + stream-K; row-parallel: all
+    stream-K, launched on every SM) covers each (tile, k-block) exactly once
+    with consistent contributor counts and slab indices."""
+    lib = pgb._lib.load()
+    bad = []
+    for T, N, K in SHAPE_SWEEP:
+        for all_sk, grid in ((0, 0), (1, sms)):
+            if lib.pgb_check_work_plan(T, N, K, sms, all_sk, grid) != 0:
+                bad.append((T, N, K, all_sk, lib.pgb_last_error().decode()))
+    assert not bad, bad[:5]
