@@ -169,6 +169,12 @@ PGB_API int pgb_rmsnorm(const void* x, const void* w, float eps, void* out, int 
  * Needs no GPU. Internal consistency check, no reference counterpart. */
 PGB_API int pgb_check_work_plan(int T, int N, int K, int sms, int all_streamk, int launch_grid);
 
+/* Launch features in effect for this process, as a bit mask: bit 0 set when
+ * kernels are launched with programmatic dependent launch (environment
+ * variable PGB_DISABLE_PDL=1 turns it off; it also turns itself off if the
+ * driver refuses it). No reference counterpart. */
+PGB_API int pgb_launch_features(void);
+
 #ifdef __cplusplus
 }
 #endif

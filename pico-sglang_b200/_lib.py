@@ -77,6 +77,7 @@ _SIGS: dict[str, tuple[object, list[object]]] = {
     "pgb_fused_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p]),
     "pgb_rmsnorm": (c_int, [c_void_p, c_void_p, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
     "pgb_check_work_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "pgb_launch_features": (c_int, []),
 }
 
 _lock = threading.Lock()

@@ -67,6 +67,7 @@ template <typename IO>
 __global__ void __launch_bounds__(256) allreduce_kernel(CommDev cm, IO* data, long long count,
                                                         long long per, int oneshot) {
   __shared__ uint32_t s_epoch;
+  pdl_wait();
   if (threadIdx.x == 0) s_epoch = comm_begin(cm);
   __syncthreads();
   const uint32_t e = s_epoch;
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__(256) allgather_kernel(CommDev cm, IO* out, con
                                                         long long count, long long out_stride,
                                                         long long out_offset) {
   __shared__ uint32_t s_epoch;
+  pdl_wait();
   if (threadIdx.x == 0) s_epoch = comm_begin(cm);
   __syncthreads();
   const uint32_t e = s_epoch;
@@ -166,13 +168,7 @@ int launch_coop(K kern, int grid, cudaStream_t s, Args... args) {
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  PGB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
-  return PGB_OK;
+  return launch_ex(cfg, /*cooperative=*/true, kern, args...);
 }
 
 int check_comm(const pgb_comm* c, const char* what) {

@@ -15,6 +15,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     col_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     GemmShape g, IO* __restrict__ y, const IO* __restrict__ bias) {
   extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_pre;  // stages armed with weight tiles before pdl_wait()
   GemmCtl c = gemm_carve_smem<BN, STAGES>(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -32,8 +33,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(c.drain, 1);
     *c.abort = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tm_a);
-    tma_prefetch_desc(&tm_b);
+    s_pre = gemm_prefetch_weights<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b,
+                                                   SWAP ? l2_policy_evict_first() : l2_policy_evict_last());
   }
   if (warp == 1) {
     tmem_alloc(c.tmem_base, 2 * BN);
@@ -42,16 +43,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (threadIdx.x == 0) pdl_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
       const uint64_t hw = l2_policy_evict_first();
       const uint64_t hx = l2_policy_evict_last();
-      gemm_producer<BN, STAGES>(g, c, &tm_a, &tm_b, SWAP ? hw : hx, SWAP ? hx : hw);
+      gemm_producer<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b, SWAP ? hw : hx, SWAP ? hx : hw, s_pre, [] {});
     }
   } else if (warp == 1) {
     if (lane == 0) gemm_mma<BN, STAGES>(g, c, umma_idesc_f16(kTileP, BN, std::is_same<IO, __nv_bfloat16>::value));
   } else {
+    pdl_wait();  // outputs may still be read by the previous kernel
     const uint32_t tmem = *c.tmem_base;
     const int row = epi_row();
     int acc = 0;
@@ -129,12 +132,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(*c.tmem_base, 2 * BN);
   }
+  pdl_wait();
+  if (threadIdx.x == 0) trace(1004);
   if (g.sk_first < g.tiles) {
     // Reduction phase: the grid finishes the shared stream-K tiles, summing
     // the contributors' partials in order. Each thread owns 4 features of a
     // (tile, token) row per step and keeps 4 steps of loads in flight.
     uint32_t* bar = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(g.status) + 64);
-    if (grid_barrier_local(bar, bar + 16, g.status, g.wait_ns)) {
+    const bool passed = grid_barrier_local(bar, bar + 16, g.status, g.wait_ns);
+    if (threadIdx.x == 0) trace(1002);
+    if (passed) {
       const long long rows = static_cast<long long>(g.tiles - g.sk_first) * g.T;
       const long long n4 = rows * 32;
       const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -238,15 +245,10 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // the reduction phase waits on every CTA
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const CUtensorMap& ta = SWAP ? tm_w : tm_x;
   const CUtensorMap& tb = SWAP ? tm_x : tm_w;
-  PGB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, g, static_cast<IO*>(y), static_cast<const IO*>(bias)));
-  return PGB_OK;
+  // The reduction phase waits on every CTA: cooperative launch.
+  return launch_ex(cfg, /*cooperative=*/true, kern, ta, tb, g, static_cast<IO*>(y), static_cast<const IO*>(bias));
 }
 
 template <typename IO>

@@ -198,34 +198,81 @@ __device__ __forceinline__ GemmCtl gemm_carve_smem(uint8_t* raw) {
   return c;
 }
 
-// Producer: one thread.
-template <int BN, int STAGES>
+// Weight tiles of the first STAGES k-blocks of this CTA into fresh stages
+// (no wait needed), issued by thread 0 right after the barriers are
+// initialised, before TMEM allocation and before the predecessor kernel
+// has finished. Returns how many stages were armed; gemm_producer adds
+// their activation tiles after pdl_wait().
+template <int BN, int STAGES, bool SWAP>
+__device__ __forceinline__ int gemm_prefetch_weights(const GemmShape& g, const GemmCtl& c,
+                                                     const CUtensorMap* tm_a, const CUtensorMap* tm_b,
+                                                     uint64_t hint_w) {
+  using L = GemmSmem<BN, STAGES>;
+  int pre = 0;
+  SegIter it0(g);
+  Seg s0;
+  while (pre < STAGES && it0.next(g, s0)) {
+    for (int kb = s0.kb0; kb < s0.kb1 && pre < STAGES; ++kb, ++pre) {
+      mbar_arrive_expect_tx(&c.full[pre], L::kStageBytes);
+      if (SWAP)
+        tma_load_2d(tm_a, &c.full[pre], c.a + pre * L::kABytes, kb * kBlockK, s0.p * kTileP, hint_w);
+      else
+        tma_load_2d(tm_b, &c.full[pre], c.b + pre * L::kBBytes, kb * kBlockK, s0.q * BN, hint_w);
+    }
+  }
+  return pre;
+}
+
+// Producer: one thread. The weight operand (A in the swap orientation, B
+// otherwise) does not depend on the previous kernel, so the first STAGES
+// k-blocks' weight tiles are requested before pdl_wait(); the activation
+// tiles of those stages follow once the predecessor has finished, then the
+// steady-state loop streams both. after_wait() runs right after pdl_wait().
+template <int BN, int STAGES, bool SWAP, typename AfterWait>
 __device__ __forceinline__ void gemm_producer(const GemmShape& g, const GemmCtl& c,
                                               const CUtensorMap* tm_a, const CUtensorMap* tm_b,
-                                              uint64_t hint_a, uint64_t hint_b) {
+                                              uint64_t hint_a, uint64_t hint_b, int pre,
+                                              AfterWait&& after_wait) {
   using L = GemmSmem<BN, STAGES>;
-  int stage = 0;
-  uint32_t phase = 0;
+  auto load_w = [&](int stage, int kb, const Seg& s) {
+    if (SWAP)
+      tma_load_2d(tm_a, &c.full[stage], c.a + stage * L::kABytes, kb * kBlockK, s.p * kTileP, hint_a);
+    else
+      tma_load_2d(tm_b, &c.full[stage], c.b + stage * L::kBBytes, kb * kBlockK, s.q * BN, hint_b);
+  };
+  auto load_x = [&](int stage, int kb, const Seg& s) {
+    if (SWAP)
+      tma_load_2d(tm_b, &c.full[stage], c.b + stage * L::kBBytes, kb * kBlockK, s.q * BN, hint_b);
+    else
+      tma_load_2d(tm_a, &c.full[stage], c.a + stage * L::kABytes, kb * kBlockK, s.p * kTileP, hint_a);
+  };
   int issued[STAGES];
 #pragma unroll
-  for (int i = 0; i < STAGES; ++i) issued[i] = -1;
+  for (int i = 0; i < STAGES; ++i) issued[i] = i < pre ? 0 : -1;
+  (void)load_w;
+  pdl_wait();
+  after_wait();
+  int stage = 0;
+  uint32_t phase = 0;
   bool ok = true;
   int n_issued = 0;
   SegIter it(g);
   Seg tc;
   while (ok && it.next(g, tc)) {
     for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
-      if (!mbar_wait(&c.empty[stage], phase ^ 1u, g.wait_ns, c.abort)) {
-        ok = false;
-        break;
+      if (n_issued < pre) {
+        load_x(stage, kb, tc);  // stage armed above
+      } else {
+        if (!mbar_wait(&c.empty[stage], phase ^ 1u, g.wait_ns, c.abort)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&c.full[stage], L::kStageBytes);
+        load_w(stage, kb, tc);
+        load_x(stage, kb, tc);
       }
       trace(n_issued < 200 ? n_issued : 1023);
       ++n_issued;
-      mbar_arrive_expect_tx(&c.full[stage], L::kStageBytes);
-      tma_load_2d(tm_a, &c.full[stage], c.a + stage * L::kABytes, kb * kBlockK, tc.p * kTileP,
-                  hint_a);
-      tma_load_2d(tm_b, &c.full[stage], c.b + stage * L::kBBytes, kb * kBlockK, tc.q * BN,
-                  hint_b);
       issued[stage] = static_cast<int>(phase);
       if (++stage == STAGES) {
         stage = 0;

@@ -1,6 +1,7 @@
 // host_common.cu - last-error handling, device properties, TMA descriptors.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -37,6 +38,14 @@ int cuda_error(cudaError_t e, const char* what) {
 }
 
 const char* last_error_cstr() { return g_last_error.c_str(); }
+
+bool& pdl_enabled() {
+  static bool on = [] {
+    const char* v = getenv("PGB_DISABLE_PDL");
+    return !(v != nullptr && v[0] == '1');
+  }();
+  return on;
+}
 
 int current_device_info(DeviceInfo* out) {
   int dev = 0;

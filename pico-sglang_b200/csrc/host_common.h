@@ -43,4 +43,39 @@ int make_tmap_2d_16bit(CUtensorMap* map, const void* base, uint64_t inner, uint6
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Whether launches request programmatic stream serialization (PDL). Cleared
+// for the process if the driver refuses a launch with it.
+bool& pdl_enabled();
+
+// Launch with cudaLaunchKernelEx: optional cooperative attribute plus PDL.
+// If the PDL combination is refused, retries once without it and keeps it
+// off for the rest of the process.
+template <typename Kern, typename... Args>
+int launch_ex(cudaLaunchConfig_t cfg, bool cooperative, Kern kern, Args... args) {
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cooperative) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
+  const bool pdl = pdl_enabled();
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess && pdl) {
+    (void)cudaGetLastError();
+    pdl_enabled() = false;
+    cfg.numAttrs = n - 1;
+    e = cudaLaunchKernelEx(&cfg, kern, args...);
+  }
+  if (e != cudaSuccess) return cuda_error(e, "cudaLaunchKernelEx");
+  return PGB_OK;
+}
+
 }  // namespace pgb

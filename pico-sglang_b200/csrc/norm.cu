@@ -19,6 +19,7 @@ __global__ void __launch_bounds__(kNormThreads) fused_add_rmsnorm_kernel(IO* x, 
                                                                          const IO* w, float eps,
                                                                          int width) {
   __shared__ float red[32];
+  pdl_wait();
   const int t = blockIdx.x;
   const int nvec = width >> 3;
   float s[kNormMaxVec][8];
@@ -57,6 +58,7 @@ template <typename IO>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const IO* x, const IO* w, float eps,
                                                                IO* out, int width) {
   __shared__ float red[32];
+  pdl_wait();
   const int t = blockIdx.x;
   const int nvec = width >> 3;
   float s[kNormMaxVec][8];
@@ -85,6 +87,15 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const IO* x, cons
 }
 
 namespace {
+template <typename K, typename... Args>
+int launch_norm(cudaStream_t s, int T, K kern, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(T);
+  cfg.blockDim = dim3(kNormThreads);
+  cfg.stream = s;
+  return launch_ex(cfg, /*cooperative=*/false, kern, args...);
+}
+
 int check_norm_args(const char* what, int T, int H, int dtype, const void* a, const void* b,
                     const void* c) {
   if (T < 0 || H <= 0) return set_error(PGB_ERR_INVALID, "%s: bad shape T=%d H=%d", what, T, H);
@@ -113,20 +124,19 @@ extern "C" int pgb_fused_add_rmsnorm(void* x, void* residual, const void* w, flo
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case PGB_BF16:
-      fused_add_rmsnorm_kernel<__nv_bfloat16><<<T, kNormThreads, 0, s>>>(
+      rc = launch_norm(s, T, fused_add_rmsnorm_kernel<__nv_bfloat16>, 
           static_cast<__nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
           static_cast<const __nv_bfloat16*>(w), eps, H);
       break;
     case PGB_F16:
-      fused_add_rmsnorm_kernel<__half><<<T, kNormThreads, 0, s>>>(
+      rc = launch_norm(s, T, fused_add_rmsnorm_kernel<__half>, 
           static_cast<__half*>(x), static_cast<__half*>(residual), static_cast<const __half*>(w), eps, H);
       break;
     default:
-      fused_add_rmsnorm_kernel<float><<<T, kNormThreads, 0, s>>>(
+      rc = launch_norm(s, T, fused_add_rmsnorm_kernel<float>, 
           static_cast<float*>(x), static_cast<float*>(residual), static_cast<const float*>(w), eps, H);
   }
-  PGB_CUDA_TRY(cudaGetLastError());
-  return PGB_OK;
+  return rc;
 }
 
 extern "C" int pgb_rmsnorm(const void* x, const void* w, float eps, void* out, int T, int H,
@@ -137,20 +147,19 @@ extern "C" int pgb_rmsnorm(const void* x, const void* w, float eps, void* out, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case PGB_BF16:
-      rmsnorm_kernel<__nv_bfloat16><<<T, kNormThreads, 0, s>>>(
+      rc = launch_norm(s, T, rmsnorm_kernel<__nv_bfloat16>, 
           static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), eps,
           static_cast<__nv_bfloat16*>(out), H);
       break;
     case PGB_F16:
-      rmsnorm_kernel<__half><<<T, kNormThreads, 0, s>>>(static_cast<const __half*>(x),
+      rc = launch_norm(s, T, rmsnorm_kernel<__half>, static_cast<const __half*>(x),
                                                        static_cast<const __half*>(w), eps,
                                                        static_cast<__half*>(out), H);
       break;
     default:
-      rmsnorm_kernel<float><<<T, kNormThreads, 0, s>>>(static_cast<const float*>(x),
+      rc = launch_norm(s, T, rmsnorm_kernel<float>, static_cast<const float*>(x),
                                                       static_cast<const float*>(w), eps,
                                                       static_cast<float*>(out), H);
   }
-  PGB_CUDA_TRY(cudaGetLastError());
-  return PGB_OK;
+  return rc;
 }

@@ -24,6 +24,7 @@ __device__ __forceinline__ uint32_t comm_begin(const CommDev& cm) {
 // all ranks' flags reached e. The wait is bounded by cm.timeout_ns and ends
 // early when another CTA already recorded an error. Every CTA must call this
 // with the same `bar` sequence, errors or not, so counters stay balanced.
+// sys_scope = false (one GPU) only synchronises the grid, at device scope.
 __device__ __forceinline__ bool grid_cross_barrier(const CommDev& cm, int bar, uint32_t e,
                                                    bool sys_scope) {
   __shared__ int s_ok;
@@ -37,15 +38,21 @@ __device__ __forceinline__ bool grid_cross_barrier(const CommDev& cm, int bar, u
     const uint32_t old = atom_add_acqrel_gpu(&cm.arrive[bar], 1u);
     if (old == gridDim.x - 1) {
       cm.arrive[bar] = 0u;
-      if (sys_scope) __threadfence_system();
-      for (int r = 0; r < cm.world; ++r) st_release_sys(&cm.flags[r][bar * PGB_MAX_RANKS + cm.rank], e);
+      if (sys_scope) {
+        __threadfence_system();
+        for (int r = 0; r < cm.world; ++r) st_release_sys(&cm.flags[r][bar * PGB_MAX_RANKS + cm.rank], e);
+      } else {  // one GPU: its own flag, device scope
+        st_release_gpu(&cm.flags[cm.rank][bar * PGB_MAX_RANKS + cm.rank], e);
+      }
     }
     volatile int* st = cm.status;
     if (*st != 0) ok = 0;
     Deadline d(cm.timeout_ns);
     const uint32_t* mine = cm.flags[cm.rank] + bar * PGB_MAX_RANKS;
-    for (int r = 0; r < cm.world && ok; ++r) {
-      while (!epoch_reached(ld_acquire_sys(mine + r), e)) {
+    const int nranks = sys_scope ? cm.world : 1;
+    for (int r0 = 0; r0 < nranks && ok; ++r0) {
+      const int r = sys_scope ? r0 : cm.rank;
+      while (!epoch_reached(sys_scope ? ld_acquire_sys(mine + r) : ld_acquire_gpu(mine + r), e)) {
         if (d.expired()) {
           record_error(cm.status, kDevTimeoutPeer);
           ok = 0;

@@ -105,7 +105,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     row_fused_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      RowArgs a) {
   extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_pre;  // stages armed with weight tiles before pdl_wait()
   __shared__ uint32_t s_epoch;
+  __shared__ uint64_t s_epoch_bar;  // the producer publishes s_epoch after pdl_wait()
   __shared__ float s_red[32];
   GemmCtl c = gemm_carve_smem<BN, STAGES>(smem_raw);
   const int warp = threadIdx.x >> 5;
@@ -113,7 +115,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const GemmShape& g = a.g;
 
   if (threadIdx.x == 0) {
-    s_epoch = comm_begin(a.cm);
+    trace(1000);
+    mbar_init(&s_epoch_bar, 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&c.full[i], 1);
       mbar_init(&c.empty[i], 1);
@@ -125,8 +128,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(c.drain, 1);
     *c.abort = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tm_a);
-    tma_prefetch_desc(&tm_b);
+    s_pre = gemm_prefetch_weights<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b,
+                                                   SWAP ? l2_policy_evict_first() : l2_policy_evict_last());
   }
   if (warp == 1) {
     tmem_alloc(c.tmem_base, 2 * BN);
@@ -135,8 +138,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t e = s_epoch;
-  const uint32_t parity = e & 1u;
+  if (threadIdx.x == 0) pdl_launch_dependents();
   // Decode plans put every tile in the stream-K part; their segments leave
   // f32 partials that the reduction phases combine.
   const bool staged = g.sk_first == 0 && g.tiles > 0;
@@ -145,11 +147,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const uint64_t hw = l2_policy_evict_first();
       const uint64_t hx = l2_policy_evict_last();
-      gemm_producer<BN, STAGES>(g, c, &tm_a, &tm_b, SWAP ? hw : hx, SWAP ? hx : hw);
+      // The epoch counter is written by the previous call on this stream:
+      // read it only once that call has finished.
+      gemm_producer<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b, SWAP ? hw : hx, SWAP ? hx : hw, s_pre, [&] {
+        s_epoch = comm_begin(a.cm);
+        mbar_arrive(&s_epoch_bar);
+      });
     }
   } else if (warp == 1) {
     if (lane == 0) gemm_mma<BN, STAGES>(g, c, umma_idesc_f16(kTileP, BN, std::is_same<IO, __nv_bfloat16>::value));
   } else {
+    pdl_wait();
+    if (!mbar_wait(&s_epoch_bar, 0u, g.wait_ns, nullptr)) record_error(g.status, kDevTimeoutPipeline);
+    const uint32_t parity = s_epoch & 1u;
     const uint32_t tmem = *c.tmem_base;
     const int row = epi_row();
     const IO* bias = static_cast<const IO*>(a.bias);
@@ -222,6 +232,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_dealloc(*c.tmem_base, 2 * BN);
   }
 
+  pdl_wait();
+  const uint32_t e = s_epoch;  // published before the barrier above
+  const uint32_t parity = e & 1u;
   const bool multi = a.cm.world > 1;
   IO* out = static_cast<IO*>(a.out);
   IO* residual = static_cast<IO*>(a.residual);
@@ -269,7 +282,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   // A failure anywhere on this GPU poisons the status; the barriers then
   // stop waiting and the later phases are skipped.
+  if (threadIdx.x == 0) trace(1004);
   const bool ok0 = grid_cross_barrier(a.cm, kBarPartials, e, multi) && ok;
+  if (threadIdx.x == 0) trace(1002);
   if (ok0) {
     const int r0 = a.rs.first(a.cm.rank), r1 = a.rs.last(a.cm.rank);
     for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x) {
@@ -285,7 +300,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool ok2 = grid_cross_barrier(a.cm, kBarResults, e, true);
     if (ok0 && ok2) gather_rows<IO>(a.cm, a.rs, parity, g.N, out, residual, a.do_norm);
   }
+  if (threadIdx.x == 0) trace(1003);
   comm_end(a.cm, e);
+  if (threadIdx.x == 0) trace(1001);
 }
 
 namespace {
@@ -312,15 +329,9 @@ int launch_row(pgb_comm* c, RowArgs args, const void* x, const void* w, cudaStre
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const CUtensorMap& ta = SWAP ? tm_w : tm_x;
   const CUtensorMap& tb = SWAP ? tm_x : tm_w;
-  PGB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, args));
-  return PGB_OK;
+  return launch_ex(cfg, /*cooperative=*/true, kern, ta, tb, args);
 }
 
 template <typename IO>
@@ -438,3 +449,10 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
   if (dtype == PGB_BF16) return dispatch_row<__nv_bfloat16>(comm, p, args, x_local, w_local, s);
   return dispatch_row<__half>(comm, p, args, x_local, w_local, s);
 }
+
+#ifdef PGB_TRACE
+extern "C" PGB_API int pgb_debug_set_trace_row(void* buf) {
+  cudaError_t e = cudaMemcpyToSymbol(pgb::pgb_trace_buf, &buf, sizeof(buf));
+  return e == cudaSuccess ? 0 : 2;
+}
+#endif

@@ -210,6 +210,18 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n, bool bf16) {
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
+// ------------------------------------------------ programmatic launch ---
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while its predecessor in the stream is still
+// running. pdl_wait() blocks until the predecessor grid has completed and
+// its memory is visible; everything that reads the predecessor's outputs
+// or writes memory it may still read must come after it. Without the
+// launch attribute both instructions are no-ops in effect.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------ misc sync ---
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
