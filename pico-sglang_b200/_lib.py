@@ -76,8 +76,9 @@ _SIGS: dict[str, tuple[object, list[object]]] = {
     ),
     "pgb_fused_add_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p]),
     "pgb_rmsnorm": (c_int, [c_void_p, c_void_p, c_float, c_void_p, c_int, c_int, c_int, c_void_p]),
-    "pgb_check_work_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "pgb_check_work_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int]),
     "pgb_launch_features": (c_int, []),
+    "pgb_describe_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_char_p, c_size_t]),
 }
 
 _lock = threading.Lock()

@@ -168,7 +168,7 @@ int launch_coop(K kern, int grid, cudaStream_t s, Args... args) {
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
-  return launch_ex(cfg, /*cooperative=*/true, kern, args...);
+  return launch_ex(cfg, /*cooperative=*/true, 1, kern, args...);
 }
 
 int check_comm(const pgb_comm* c, const char* what) {

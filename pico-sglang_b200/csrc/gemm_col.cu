@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     trace(1000);
+    tma_prefetch_desc(&tm_a);  // descriptor fetch overlaps barrier set-up
+    tma_prefetch_desc(&tm_b);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&c.full[i], 1);
       mbar_init(&c.empty[i], 1);
@@ -31,10 +33,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(&c.acc_empty[0], kEpiThreads);
     mbar_init(&c.acc_empty[1], kEpiThreads);
     mbar_init(c.drain, 1);
+    mbar_init(c.red_ready, g.csk > 1 ? g.csk : 1);
+    mbar_init(c.red_free, g.csk > 1 ? g.csk : 1);
     *c.abort = 0;
     fence_mbar_init();
+    trace(1005);
     s_pre = gemm_prefetch_weights<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b,
                                                    SWAP ? l2_policy_evict_first() : l2_policy_evict_last());
+    trace(1006);
   }
   if (warp == 1) {
     tmem_alloc(c.tmem_base, 2 * BN);
@@ -43,6 +49,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (g.csk > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   if (threadIdx.x == 0) pdl_launch_dependents();
 
   if (warp == 0) {
@@ -61,6 +68,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t acc_phase = 0;
     int n_units = 0;
     (void)n_units;
+    uint32_t red_seq = 0;
     SegIter it(g);
     Seg tc;
     while (it.next(g, tc)) {
@@ -71,7 +79,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after();
       if (threadIdx.x == 64) trace(400 + (n_units < 32 ? n_units : 31));
-      if (tc.nctb > 1) {
+      if (g.csk > 1) {
+        // Cluster split-K: sum the cluster's partials on chip and store.
+        cluster_reduce_tile<BN>(g, tc, c, tmem, acc, red_seq, [&](int t, int n0, float4 v) {
+          if (bias != nullptr) {
+            v.x += io_to_f32<IO>(bias[n0]);
+            v.y += io_to_f32<IO>(bias[n0 + 1]);
+            v.z += io_to_f32<IO>(bias[n0 + 2]);
+            v.w += io_to_f32<IO>(bias[n0 + 3]);
+          }
+          IO h[4] = {f32_to_io<IO>(v.x), f32_to_io<IO>(v.y), f32_to_io<IO>(v.z), f32_to_io<IO>(v.w)};
+          *reinterpret_cast<uint2*>(y + static_cast<size_t>(t) * g.N + n0) = *reinterpret_cast<uint2*>(h);
+        });
+      } else if (tc.nctb > 1) {
         // Shared tile: leave an f32 partial for the reduction phase.
         partial_store_tm<BN>(g, tc, tmem, acc);
       } else {
@@ -124,6 +144,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    cluster_reduce_drain(g, c, red_seq);
   }
 
   tc_fence_before();
@@ -134,7 +155,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   pdl_wait();
   if (threadIdx.x == 0) trace(1004);
-  if (g.sk_first < g.tiles) {
+  if (g.csk <= 1 && g.sk_first < g.tiles) {
     // Reduction phase: the grid finishes the shared stream-K tiles, summing
     // the contributors' partials in order. Each thread owns 4 features of a
     // (tile, token) row per step and keeps 4 steps of loads in flight.
@@ -203,8 +224,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 namespace {
 
 template <typename IO, int BN, bool SWAP>
-int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
-               const void* bias, void* y, int T, int N, int K, uint8_t* ws, cudaStream_t stream) {
+int launch_col(const GemmPlan& p0, const DeviceInfo& dev, const void* x, const void* w,
+               const void* bias, void* y, int T, int N, int K, uint8_t* ws, size_t ws_bytes,
+               cudaStream_t stream) {
   constexpr int STAGES = gemm_stages<BN>();
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kBytes <= 232448, "shared memory budget");
@@ -213,6 +235,15 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
     return set_error(PGB_ERR_UNSUPPORTED, "kernel needs %d B shared memory, device allows %d",
                      L::kBytes, dev.max_smem_optin);
   PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  // Re-plan with the cluster sizes this kernel can actually co-schedule.
+  ClusterCaps caps;
+  query_cluster_caps(kern, kGemmThreads, L::kBytes, caps.max_active);
+  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, SIZE_MAX, false, &caps);
+  if (p.bn != p0.bn || p.swap != p0.swap)
+    return set_error(PGB_ERR_STATE, "col_gemm: inconsistent plan");
+  if (col_workspace_bytes(p) > ws_bytes)
+    return set_error(PGB_ERR_INVALID, "col_gemm: workspace of %zu bytes, %zu needed", ws_bytes,
+                     col_workspace_bytes(p));
 
   constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
   CUtensorMap tm_x, tm_w;
@@ -236,31 +267,34 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
   g.grid = p.grid;
   g.sk_grid = p.sk_grid;
   g.max_contrib = p.max_contrib;
+  g.csk = p.csk;
+  g.n_clusters = p.n_clusters;
   g.status = reinterpret_cast<int*>(ws);
   g.ws = reinterpret_cast<float*>(ws + kWsHeaderBytes);
   g.wait_ns = 2000000000ull;  // 2 s: far beyond any legitimate pipeline stall
 
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(p.grid);
+  cfg.gridDim = dim3(p.grid);  // n_clusters * csk for cluster split-K
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   const CUtensorMap& ta = SWAP ? tm_w : tm_x;
   const CUtensorMap& tb = SWAP ? tm_x : tm_w;
   // The reduction phase waits on every CTA: cooperative launch.
-  return launch_ex(cfg, /*cooperative=*/true, kern, ta, tb, g, static_cast<IO*>(y), static_cast<const IO*>(bias));
+  return launch_ex(cfg, /*cooperative=*/p.csk <= 1, p.csk, kern, ta, tb, g, static_cast<IO*>(y),
+                   static_cast<const IO*>(bias));
 }
 
 template <typename IO>
 int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
-                 const void* bias, void* y, int T, int N, int K, uint8_t* ws,
+                 const void* bias, void* y, int T, int N, int K, uint8_t* ws, size_t wsb,
                  cudaStream_t stream) {
-  if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, bias, y, T, N, K, ws, stream);
+  if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
   switch (p.bn) {
-    case 32: return launch_col<IO, 32, true>(p, dev, x, w, bias, y, T, N, K, ws, stream);
-    case 64: return launch_col<IO, 64, true>(p, dev, x, w, bias, y, T, N, K, ws, stream);
-    case 128: return launch_col<IO, 128, true>(p, dev, x, w, bias, y, T, N, K, ws, stream);
-    case 256: return launch_col<IO, 256, true>(p, dev, x, w, bias, y, T, N, K, ws, stream);
+    case 32: return launch_col<IO, 32, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+    case 64: return launch_col<IO, 64, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+    case 128: return launch_col<IO, 128, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+    case 256: return launch_col<IO, 256, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
     default: return set_error(PGB_ERR_INVALID, "no kernel for tile width %d", p.bn);
   }
 }
@@ -306,8 +340,8 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
                      need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  if (dtype == PGB_BF16) return dispatch_col<__nv_bfloat16>(p, dev, x, w, bias, y, T, N, K, ws, s);
-  return dispatch_col<__half>(p, dev, x, w, bias, y, T, N, K, ws, s);
+  if (dtype == PGB_BF16) return dispatch_col<__nv_bfloat16>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
+  return dispatch_col<__half>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
 }
 
 #ifdef PGB_TRACE

@@ -51,6 +51,12 @@ constexpr int kMaxRanks = 8;
 // finished after a grid barrier (cooperative launch) by all warps together,
 // adding the contributors' f32 partials in contributor order, so the result
 // does not depend on timing.
+//
+// Cluster split-K (csk > 1) replaces both: the grid is made of clusters of
+// csk CTAs, cluster c computes tiles c, c + n_clusters, ..., and CTA r of the
+// cluster streams k-blocks [r*kblocks/csk, (r+1)*kblocks/csk) of each. The
+// csk partial accumulators are summed through distributed shared memory
+// (cluster_reduce_tile), so no partial leaves the chip.
 struct GemmShape {
   int T, N, K;
   int kblocks;      // ceil(K / 64)
@@ -63,6 +69,8 @@ struct GemmShape {
   int sk_grid;      // CTAs taking part in the stream-K part, <= grid and <=
                     // its k-block count, so every stream-K range is non-empty
   int max_contrib;  // partial slabs reserved per stream-K tile
+  int csk;          // > 1: cluster split-K with this cluster size (see SegIter)
+  int n_clusters;   // clusters in the launch when csk > 1
   float* ws;        // partials [tiles - sk_first][max_contrib][BN tokens][128 features] f32
   int* status;      // device status word (first error wins); the grid
                     // barrier's counters follow it at +64 and +128 bytes
@@ -92,8 +100,19 @@ __host__ __device__ __forceinline__ long long streamk_total(const GemmShape& g) 
 struct SegIter {
   long long u, u1, total;
   int t, round, cta;
+  int ckb0, ckb1;  // cluster split-K: this CTA's k-range of every tile
   __host__ __device__ __forceinline__ SegIter(const GemmShape& g, int cta_) {
     cta = cta_;
+    if (g.csk > 1) {
+      const int cl = cta / g.csk, r = cta % g.csk;
+      t = cl < g.n_clusters ? cl : g.tiles;
+      ckb0 = r * g.kblocks / g.csk;
+      ckb1 = (r + 1) * g.kblocks / g.csk;
+      round = 0;
+      u = u1 = total = 0;
+      return;
+    }
+    ckb0 = ckb1 = 0;
     total = streamk_total(g);
     round = 0;
     t = cta;
@@ -107,6 +126,18 @@ struct SegIter {
   }
   __device__ __forceinline__ explicit SegIter(const GemmShape& g) : SegIter(g, static_cast<int>(blockIdx.x)) {}
   __host__ __device__ __forceinline__ bool next(const GemmShape& g, Seg& s) {
+    if (g.csk > 1) {
+      if (t >= g.tiles) return false;
+      s.tile = t;
+      s.kb0 = ckb0;
+      s.kb1 = ckb1;
+      s.contrib = cta % g.csk;
+      s.nctb = g.csk;
+      s.p = t % g.p_tiles;
+      s.q = t / g.p_tiles;
+      t += g.n_clusters;
+      return true;
+    }
     if (round < g.dp_rounds) {
       s.tile = t + round * g.grid;
       ++round;
@@ -150,15 +181,17 @@ struct GemmSmem {
   static constexpr int kOffB = STAGES * kABytes;
   static constexpr int kOffEpi = kOffB + STAGES * kBBytes;
   static constexpr int kEpiBytes = 32 * kTileP * 2;  // 32 tokens x 128 features, 16-bit
-  static constexpr int kOffBar = kOffEpi + kEpiBytes;
-  static constexpr int kBarBytes = 8 * (2 * STAGES + 5) + 64;
+  static constexpr int kOffRed = kOffEpi + kEpiBytes;
+  static constexpr int kRedBytes = 32 * kTileP * 4;  // cluster split-K chunk: 32 tokens x 128 f32
+  static constexpr int kOffBar = kOffRed + kRedBytes;
+  static constexpr int kBarBytes = 8 * (2 * STAGES + 7) + 64;
   static constexpr int kBytes = kOffBar + kBarBytes + 1024;  // + alignment slack
 };
 
 // Pipeline depth that fills the shared-memory budget for a tile width.
 template <int BN>
 constexpr int gemm_stages() {
-  constexpr int kBudget = 216 * 1024;  // leaves room for the epilogue tile and barriers
+  constexpr int kBudget = 200 * 1024;  // leaves room for the epilogue tiles and barriers
   constexpr int kStage = kTileP * kBlockK * 2 + BN * kBlockK * 2;
   return kBudget / kStage > 12 ? 12 : kBudget / kStage;
 }
@@ -175,6 +208,9 @@ struct GemmCtl {
   uint8_t* a;
   uint8_t* b;
   uint16_t* epi;  // [32][128] staging tile of the swap-orientation epilogue
+  float* red;     // [32][128] f32 chunk exchanged by cluster split-K
+  uint64_t* red_ready;  // all csk chunks of the cluster are written
+  uint64_t* red_free;   // all csk CTAs finished reading this CTA's chunk
 };
 
 template <int BN, int STAGES>
@@ -186,13 +222,16 @@ __device__ __forceinline__ GemmCtl gemm_carve_smem(uint8_t* raw) {
   c.a = base + L::kOffA;
   c.b = base + L::kOffB;
   c.epi = reinterpret_cast<uint16_t*>(base + L::kOffEpi);
+  c.red = reinterpret_cast<float*>(base + L::kOffRed);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::kOffBar);
   c.full = bars;
   c.empty = bars + STAGES;
   c.acc_full = bars + 2 * STAGES;
   c.acc_empty = bars + 2 * STAGES + 2;
   c.drain = bars + 2 * STAGES + 4;
-  c.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  c.red_ready = bars + 2 * STAGES + 5;
+  c.red_free = bars + 2 * STAGES + 6;
+  c.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
   c.abort = reinterpret_cast<int*>(c.tmem_base + 1);
   c.flag = c.abort + 1;
   return c;
@@ -426,6 +465,7 @@ __device__ __forceinline__ void epi_load_chunk(uint32_t tmem, int acc, int col, 
 
 // Number of CTAs contributing to `tile` (1 for whole tiles).
 __host__ __device__ __forceinline__ int tile_contributors(const GemmShape& g, int tile) {
+  if (g.csk > 1) return g.csk;
   if (tile < g.sk_first) return 1;
   const long long total = streamk_total(g);
   const long long first = static_cast<long long>(tile - g.sk_first) * g.kblocks;
@@ -502,6 +542,95 @@ __device__ __forceinline__ bool grid_barrier_local(uint32_t* arrive, uint32_t* g
   }
   __syncthreads();
   return s_ok != 0;
+}
+
+// Cluster split-K reduction of one tile (swap orientation). Every one of the
+// 128 epilogue threads of every CTA of the cluster calls this for the same
+// tile, with its own partial accumulator `acc`. Per 32-token chunk: each CTA
+// writes its partial to its shared `red` buffer (token-major), signals the
+// cluster, then reduces its share of the feature groups over the csk buffers
+// in CTA-rank order through DSMEM and hands every finished 4-feature piece to
+// emit(t, n0, float4), then signals that it is done reading. `seq` counts
+// chunks across tiles (mbarrier parities). Only the epilogue warps take part,
+// so the producer and MMA warps keep streaming the next tile meanwhile.
+template <int BN, typename Emit4>
+__device__ __forceinline__ bool cluster_reduce_tile(const GemmShape& g, const Seg& sg, const GemmCtl& c,
+                                                    uint32_t tmem, int acc, uint32_t& seq, Emit4&& emit) {
+  const int C = g.csk;
+  const int rank = static_cast<int>(blockIdx.x) % C;
+  const int row = epi_row();
+  const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
+  const int g0 = rank * (kTileP / 4) / C, g1 = (rank + 1) * (kTileP / 4) / C;
+  const int ng = g1 - g0;
+  bool ok = true;
+#pragma unroll 1
+  for (int col = 0; col < BN; col += 32) {
+    if (seq > 0 && !mbar_wait_cluster(c.red_free, (seq - 1) & 1u, g.wait_ns)) ok = false;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, col), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) c.red[j * kTileP + row] = __uint_as_float(r[j]);
+    named_bar_sync(1, kEpiThreads);
+    // One thread per destination CTA arrives, so the C release-arrives are in
+    // flight together; each releases at cluster scope, and the named barrier
+    // above orders every thread's buffer writes before it.
+    if (tid == 0) trace(1010);
+    if (tid < C) mbar_arrive_cluster(dsmem_addr(c.red_ready, tid));
+    if (tid == 0) trace(1011);
+    if (!mbar_wait_cluster(c.red_ready, seq & 1u, g.wait_ns)) ok = false;
+    if (tid == 0) trace(1012);
+    if (ok) {
+      const int items = 32 * ng;
+      for (int it0 = tid; it0 < items; it0 += 2 * kEpiThreads) {
+        // Two items per pass: all 2*C DSMEM loads in flight before the adds.
+        float4 v[2][8];
+        int jj[2], gg[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int it = it0 + k * kEpiThreads;
+          jj[k] = it < items ? it / ng : -1;
+          gg[k] = it < items ? g0 + it % ng : 0;
+          if (jj[k] >= 0) {
+            const float* my = c.red + jj[k] * kTileP + gg[k] * 4;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              if (q < C) v[k][q] = ld_dsmem_f4(dsmem_addr(my, q));
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          if (jj[k] < 0) continue;
+          float4 a = v[k][0];
+#pragma unroll
+          for (int q = 1; q < 8; ++q) {
+            if (q < C) {
+              a.x += v[k][q].x;
+              a.y += v[k][q].y;
+              a.z += v[k][q].z;
+              a.w += v[k][q].w;
+            }
+          }
+          const int t = sg.q * BN + col + jj[k], n0 = sg.p * kTileP + gg[k] * 4;
+          if (t < g.T && n0 < g.N) emit(t, n0, a);
+        }
+      }
+    }
+    named_bar_sync(1, kEpiThreads);
+    if (tid == 0) trace(1013);
+    if (tid < C) mbar_arrive_cluster(dsmem_addr(c.red_free, tid));
+    ++seq;
+  }
+  if (!ok) record_error(g.status, kDevTimeoutPipeline);
+  return ok;
+}
+
+// Before a CTA of a split-K cluster retires, every CTA of the cluster must
+// have finished reading its reduction buffer.
+__device__ __forceinline__ void cluster_reduce_drain(const GemmShape& g, const GemmCtl& c, uint32_t seq) {
+  if (g.csk > 1 && seq > 0 && !mbar_wait_cluster(c.red_free, (seq - 1) & 1u, g.wait_ns))
+    record_error(g.status, kDevTimeoutPipeline);
+  if (threadIdx.x == kGemmThreads - kEpiThreads) trace(1014);
 }
 
 // Swap orientation: this thread holds v[j] = out(feature p*128 + row,

@@ -93,7 +93,7 @@ int launch_norm(cudaStream_t s, int T, K kern, Args... args) {
   cfg.gridDim = dim3(T);
   cfg.blockDim = dim3(kNormThreads);
   cfg.stream = s;
-  return launch_ex(cfg, /*cooperative=*/false, kern, args...);
+  return launch_ex(cfg, /*cooperative=*/false, 1, kern, args...);
 }
 
 int check_norm_args(const char* what, int T, int H, int dtype, const void* a, const void* b,

@@ -58,6 +58,24 @@ __device__ __forceinline__ void row_store_partial(const RowArgs& a, uint32_t par
   }
 }
 
+// 4 consecutive features [n0, n0 + 4) of token t into the reducing rank(s).
+template <typename IO>
+__device__ __forceinline__ void row_store4(const RowArgs& a, uint32_t parity, int t, int n0, uint2 piece) {
+  const int H = a.g.N;
+  const size_t src_off = static_cast<size_t>(a.cm.rank) * a.rs.rows_cap * H;
+  int d0 = 0, d1 = a.cm.world;
+  size_t row = static_cast<size_t>(t);
+  if (!a.rs.oneshot) {
+    d0 = t / a.rs.rows_per;
+    d1 = d0 + 1;
+    row = static_cast<size_t>(t - d0 * a.rs.rows_per);
+  }
+  for (int d = d0; d < d1; ++d) {
+    IO* base = reinterpret_cast<IO*>(a.cm.slots[d] + parity * a.cm.slot_parity_bytes);
+    *reinterpret_cast<uint2*>(base + src_off + row * H + n0) = piece;
+  }
+}
+
 // 8 consecutive features [n0, n0 + 8) of token t into the reducing rank(s).
 template <typename IO>
 __device__ __forceinline__ void row_store_piece(const RowArgs& a, uint32_t parity, int t, int n0,
@@ -116,6 +134,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     trace(1000);
+    tma_prefetch_desc(&tm_a);  // descriptor fetch overlaps barrier set-up
+    tma_prefetch_desc(&tm_b);
     mbar_init(&s_epoch_bar, 1);
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&c.full[i], 1);
@@ -126,10 +146,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(&c.acc_empty[0], kEpiThreads);
     mbar_init(&c.acc_empty[1], kEpiThreads);
     mbar_init(c.drain, 1);
+    mbar_init(c.red_ready, g.csk > 1 ? g.csk : 1);
+    mbar_init(c.red_free, g.csk > 1 ? g.csk : 1);
     *c.abort = 0;
     fence_mbar_init();
+    trace(1005);
     s_pre = gemm_prefetch_weights<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b,
                                                    SWAP ? l2_policy_evict_first() : l2_policy_evict_last());
+    trace(1006);
   }
   if (warp == 1) {
     tmem_alloc(c.tmem_base, 2 * BN);
@@ -138,10 +162,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (g.csk > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   if (threadIdx.x == 0) pdl_launch_dependents();
   // Decode plans put every tile in the stream-K part; their segments leave
   // f32 partials that the reduction phases combine.
-  const bool staged = g.sk_first == 0 && g.tiles > 0;
+  const bool staged = g.csk <= 1 && g.sk_first == 0 && g.tiles > 0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -164,6 +189,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row = epi_row();
     const IO* bias = static_cast<const IO*>(a.bias);
     (void)row;
+    uint32_t red_seq = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     SegIter it(g);
@@ -175,7 +201,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      if (staged) {
+      if (g.csk > 1) {
+        // Cluster split-K: sum the cluster's partials on chip, round to the
+        // I/O type and store into the slots of the reducing rank(s).
+        cluster_reduce_tile<BN>(g, tc, c, tmem, acc, red_seq, [&](int t, int n0, float4 v) {
+          if (bias != nullptr) {
+            v.x += io_to_f32<IO>(bias[n0]);
+            v.y += io_to_f32<IO>(bias[n0 + 1]);
+            v.z += io_to_f32<IO>(bias[n0 + 2]);
+            v.w += io_to_f32<IO>(bias[n0 + 3]);
+          }
+          IO h[4] = {f32_to_io<IO>(v.x), f32_to_io<IO>(v.y), f32_to_io<IO>(v.z), f32_to_io<IO>(v.w)};
+          row_store4<IO>(a, parity, t, n0, *reinterpret_cast<uint2*>(h));
+        });
+      } else if (staged) {
         // Decode: every segment leaves an f32 token-major partial; the
         // reduction phases below combine contributors, ranks and residual.
         partial_store_tm<BN>(g, tc, tmem, acc);
@@ -223,6 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc_phase ^= 1u;
       }
     }
+    cluster_reduce_drain(g, c, red_seq);
   }
 
   tc_fence_before();
@@ -248,11 +288,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int n = tile_contributors(g, tile);
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = 0.f;
-    for (int j = 0; j < n; ++j) {
-      float p[8];
-      load8<float>(partial_tm<BN>(g, tile, j) + static_cast<size_t>(t) * kTileP + (n0 % kTileP), p);
+    const float* base = partial_tm<BN>(g, tile, 0) + static_cast<size_t>(t) * kTileP + (n0 % kTileP);
+    const size_t slab = static_cast<size_t>(BN) * kTileP;
+    // Batches of up to 8 contributors: all loads of a batch in flight
+    // before the first add; the adds stay in contributor order.
+    for (int j0 = 0; j0 < n; j0 += 8) {
+      float4 lo[8], hi[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] += p[q];
+      for (int k = 0; k < 8; ++k) {
+        if (j0 + k < n) {
+          const float4* src = reinterpret_cast<const float4*>(base + (j0 + k) * slab);
+          lo[k] = __ldcg(src);
+          hi[k] = __ldcg(src + 1);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (j0 + k < n) {
+          o[0] += lo[k].x; o[1] += lo[k].y; o[2] += lo[k].z; o[3] += lo[k].w;
+          o[4] += hi[k].x; o[5] += hi[k].y; o[6] += hi[k].z; o[7] += hi[k].w;
+        }
+      }
     }
     if (bias != nullptr) {
       float b[8];
@@ -314,6 +370,20 @@ int launch_row(pgb_comm* c, RowArgs args, const void* x, const void* w, cudaStre
   static_assert(L::kBytes + 256 <= 232448, "shared memory budget");
   auto kern = row_fused_kernel<IO, BN, SWAP, STAGES>;
   PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  // Re-plan with the cluster sizes this kernel can co-schedule.
+  {
+    ClusterCaps caps;
+    query_cluster_caps(kern, kGemmThreads, L::kBytes, caps.max_active);
+    const GemmPlan p = plan_gemm(args.g.T, args.g.N, args.g.K, c->sm_count, kSplitScratchBytes, true, &caps,
+                                 true);
+    args.g.dp_rounds = p.dp_rounds;
+    args.g.sk_first = p.sk_first;
+    args.g.grid = p.grid;
+    args.g.sk_grid = p.sk_grid;
+    args.g.max_contrib = p.max_contrib;
+    args.g.csk = p.csk;
+    args.g.n_clusters = p.n_clusters;
+  }
   constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
   const int T = args.g.T, N = args.g.N, K = args.g.K;
   CUtensorMap tm_x, tm_w;
@@ -325,13 +395,15 @@ int launch_row(pgb_comm* c, RowArgs args, const void* x, const void* w, cudaStre
   if (rc) return rc;
 
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(c->sm_count);
+  // Every SM takes part in the reduction phases; a cluster split-K launch
+  // has exactly n_clusters * csk CTAs.
+  cfg.gridDim = dim3(args.g.csk > 1 ? args.g.n_clusters * args.g.csk : c->sm_count);
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   const CUtensorMap& ta = SWAP ? tm_w : tm_x;
   const CUtensorMap& tb = SWAP ? tm_x : tm_w;
-  return launch_ex(cfg, /*cooperative=*/true, kern, ta, tb, args);
+  return launch_ex(cfg, /*cooperative=*/true, args.g.csk, kern, ta, tb, args);
 }
 
 template <typename IO>
@@ -433,6 +505,8 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
   args.g.grid = p.grid;
   args.g.sk_grid = p.sk_grid;
   args.g.max_contrib = p.max_contrib;
+  args.g.csk = p.csk;
+  args.g.n_clusters = p.n_clusters;
   args.g.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
   args.g.ws = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
   args.grid_bar = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kGridBar);

@@ -90,12 +90,14 @@ SHAPE_SWEEP = [
 @pytest.mark.parametrize("sms", [148, 132, 7])
 def test_work_decomposition_covers_every_k_block_once(pgb, sms):
     """Every planned GEMM (column: round-robin + stream-K; row-parallel: all
-    stream-K, launched on every SM) covers each (tile, k-block) exactly once
-    with consistent contributor counts and slab indices."""
+    stream-K, launched on every SM; with and without cluster split-K) covers
+    each (tile, k-block) exactly once with consistent contributor counts and
+    slab indices."""
     lib = pgb._lib.load()
     bad = []
     for T, N, K in SHAPE_SWEEP:
         for all_sk, grid in ((0, 0), (1, sms)):
-            if lib.pgb_check_work_plan(T, N, K, sms, all_sk, grid) != 0:
-                bad.append((T, N, K, all_sk, lib.pgb_last_error().decode()))
+            for clusters in (0, 1):
+                if lib.pgb_check_work_plan(T, N, K, sms, all_sk, grid, clusters) != 0:
+                    bad.append((T, N, K, all_sk, clusters, lib.pgb_last_error().decode()))
     assert not bad, bad[:5]
