@@ -130,6 +130,24 @@ PGB_API size_t pgb_col_gemm_workspace_size(int T, int N, int K);
 PGB_API int pgb_col_gemm(const void* x, const void* w, const void* bias, void* y, int T, int N, int K,
                  int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the fixed per-device scratch used by pgb_col_gemm_noalloc. */
+#define PGB_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* pgb_col_gemm without a caller workspace and without any allocation. It has
+ * no counterpart in the reference; it is for callers that cannot allocate
+ * device memory when they run the GEMM (a runtime whose HBM is already given
+ * to its KV-cache pool, an allocator hook, a latency path where cudaMalloc
+ * would synchronise). The scratch is a fixed array of
+ * PGB_NOALLOC_SCRATCH_BYTES in the library's device image, one per device:
+ *  - shapes whose plan needs more scratch return PGB_ERR_INVALID;
+ *  - all calls on a device share it, so calls whose GPU work overlaps
+ *    (unordered streams) race and give wrong results;
+ *  - the first call on each device looks up the scratch address, so make it
+ *    before any stream capture.
+ * Arguments and results are those of pgb_col_gemm. */
+PGB_API int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bias, void* y, int T, int N,
+                                 int K, int dtype, void* stream);
+
 /* Row-parallel GEMM fused with the all-reduce and the residual-add + RMSNorm
  * that consumes it:
  *   p_r      = x_local[T, K_local] . w_local[N, K_local]^T (+ bias) on rank r

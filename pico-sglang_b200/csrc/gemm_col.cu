@@ -344,6 +344,87 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
   return dispatch_col<__half>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free column GEMM.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// GEMM. Examples are a serving runtime that has already handed nearly all of
+// HBM to its KV-cache pool, an allocator hook that must not re-enter the
+// allocator, and code on a latency path where cudaMalloc/cudaFree would
+// synchronise the device. pgb_col_gemm_noalloc serves them: its stream-K
+// scratch is a fixed array inside this library's device image, so the call
+// itself allocates nothing.
+//
+// Limits and rules:
+//  - The scratch is PGB_NOALLOC_SCRATCH_BYTES per device. A shape whose plan
+//    needs more is refused with PGB_ERR_INVALID.
+//  - All calls on one device share that scratch. Two calls whose GPU work
+//    overlaps (different streams, no ordering between them) race on it and
+//    give wrong results. Order them on one stream, or use pgb_col_gemm with a
+//    workspace per stream.
+//  - The first call on each device looks up the array's device address
+//    (cudaGetSymbolAddress, with that device current). Make that first call
+//    before any stream capture.
+// ---------------------------------------------------------------------------
+
+static __device__ __align__(256) uint8_t pgb_noalloc_scratch[PGB_NOALLOC_SCRATCH_BYTES];
+
+namespace pgb {
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+
+// Device address of pgb_noalloc_scratch on the current device; looked up once
+// per device and cached.
+int noalloc_scratch(uint8_t** out) {
+  static std::mutex mu;
+  static void* addr[kNoAllocMaxDevices] = {};
+  int dev = 0;
+  PGB_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm_noalloc: device ordinal %d above %d", dev,
+                     kNoAllocMaxDevices - 1);
+  std::lock_guard<std::mutex> lk(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, pgb_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(pgb_noalloc_scratch)");
+    if (p == nullptr) return set_error(PGB_ERR_CUDA, "col_gemm_noalloc: null scratch address");
+    addr[dev] = p;
+  }
+  *out = static_cast<uint8_t*>(addr[dev]);
+  return PGB_OK;
+}
+
+}  // namespace
+}  // namespace pgb
+
+extern "C" int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bias, void* y, int T,
+                                    int N, int K, int dtype, void* stream) {
+  using namespace pgb;
+  if (T < 0 || N <= 0 || K <= 0)
+    return set_error(PGB_ERR_INVALID, "col_gemm_noalloc: bad shape T=%d N=%d K=%d", T, N, K);
+  if (T == 0) return PGB_OK;
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, SIZE_MAX);
+  const size_t need = col_workspace_bytes(p);
+  if (need > PGB_NOALLOC_SCRATCH_BYTES)
+    return set_error(PGB_ERR_INVALID,
+                     "col_gemm_noalloc: T=%d N=%d K=%d needs %zu bytes of scratch, above the fixed "
+                     "%zu; call pgb_col_gemm with a workspace instead",
+                     T, N, K, need, static_cast<size_t>(PGB_NOALLOC_SCRATCH_BYTES));
+  uint8_t* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // The header (status word and grid-barrier counters) must start at zero;
+  // the partial slabs behind it are written before they are read.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  PGB_CUDA_TRY(cudaMemsetAsync(scratch, 0, kWsHeaderBytes, s));
+  return pgb_col_gemm(x, w, bias, y, T, N, K, dtype, scratch, PGB_NOALLOC_SCRATCH_BYTES, stream);
+}
+
 #ifdef PGB_TRACE
 // Work-build only: point this translation unit's trace buffer at `buf`.
 extern "C" PGB_API int pgb_debug_set_trace(void* buf) {
