@@ -131,7 +131,7 @@ PGB_API int pgb_col_gemm(const void* x, const void* w, const void* bias, void* y
                  int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Size of the fixed per-device scratch used by pgb_col_gemm_noalloc. */
-#define PGB_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+#define PGB_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
 /* pgb_col_gemm without a caller workspace and without any allocation. It has
  * no counterpart in the reference; it is for callers that cannot allocate

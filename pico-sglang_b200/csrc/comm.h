@@ -34,7 +34,7 @@ constexpr int kNumBars = 4;          // flags per rank: barrier ids 0..3
 constexpr size_t kHeaderBytes = 4096;
 constexpr size_t kFlagBytes = 4096;
 constexpr uint64_t kCommMagic = 0x3030324247504255ull;  // layout tag
-constexpr size_t kSplitScratchBytes = 32u << 20;        // split-K partials per comm
+constexpr size_t kSplitScratchBytes = 32u << 20;        // split-tile exchange area per comm
 constexpr size_t kTileCounterBytes = 64u << 10;
 
 struct CommHeader {
@@ -53,8 +53,7 @@ struct LocalLayout {
   static constexpr size_t kStatus = 0;      // int
   static constexpr size_t kEpoch = 64;      // uint32
   static constexpr size_t kArrive = 128;    // uint32[kNumBars]
-  static constexpr size_t kGridBar = 256;   // uint32 arrive at +0, generation at +64
-  static constexpr size_t kCounters = 4096; // split-K tile counters
+  static constexpr size_t kCounters = 4096; // split-tile counters (zero at rest)
   static constexpr size_t kPartials = kCounters + kTileCounterBytes;
   static constexpr size_t kBytes = kPartials + kSplitScratchBytes;
 };

@@ -33,8 +33,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(&c.acc_empty[0], kEpiThreads);
     mbar_init(&c.acc_empty[1], kEpiThreads);
     mbar_init(c.drain, 1);
-    mbar_init(c.red_ready, g.csk > 1 ? g.csk : 1);
-    mbar_init(c.red_free, g.csk > 1 ? g.csk : 1);
+    mbar_init(c.xchg, 1);
     *c.abort = 0;
     fence_mbar_init();
     trace(1005);
@@ -49,7 +48,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (g.csk > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   if (threadIdx.x == 0) pdl_launch_dependents();
 
   if (warp == 0) {
@@ -61,14 +59,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) gemm_mma<BN, STAGES>(g, c, umma_idesc_f16(kTileP, BN, std::is_same<IO, __nv_bfloat16>::value));
   } else {
-    pdl_wait();  // outputs may still be read by the previous kernel
+    pdl_wait();  // outputs (and the exchange area) may still be read by the previous kernel
     const uint32_t tmem = *c.tmem_base;
     const int row = epi_row();
     int acc = 0;
     uint32_t acc_phase = 0;
-    int n_units = 0;
-    (void)n_units;
-    uint32_t red_seq = 0;
     SegIter it(g);
     Seg tc;
     while (it.next(g, tc)) {
@@ -78,22 +73,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      if (threadIdx.x == 64) trace(400 + (n_units < 32 ? n_units : 31));
-      if (g.csk > 1) {
-        // Cluster split-K: sum the cluster's partials on chip and store.
-        cluster_reduce_tile<BN>(g, tc, c, tmem, acc, red_seq, [&](int t, int n0, float4 v) {
-          if (bias != nullptr) {
-            v.x += io_to_f32<IO>(bias[n0]);
-            v.y += io_to_f32<IO>(bias[n0 + 1]);
-            v.z += io_to_f32<IO>(bias[n0 + 2]);
-            v.w += io_to_f32<IO>(bias[n0 + 3]);
-          }
-          IO h[4] = {f32_to_io<IO>(v.x), f32_to_io<IO>(v.y), f32_to_io<IO>(v.z), f32_to_io<IO>(v.w)};
-          *reinterpret_cast<uint2*>(y + static_cast<size_t>(t) * g.N + n0) = *reinterpret_cast<uint2*>(h);
+      if (tc.nctb > 1) {
+        // Split tile: reduce-scatter with the tile's other CTAs through L2.
+        const int N = g.N;
+        split_reduce_tile<IO, BN>(g, tc, c, tmem, acc, bias, [&](int t, int n0, uint4 piece) {
+          *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
         });
-      } else if (tc.nctb > 1) {
-        // Shared tile: leave an f32 partial for the reduction phase.
-        partial_store_tm<BN>(g, tc, tmem, acc);
       } else {
 #pragma unroll 1
         for (int col = 0; col < BN; col += 32) {
@@ -109,7 +94,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               for (int j = 0; j < 32; ++j) v[j] += b;
             }
             const int N = g.N;
-            swap_epilogue_store<IO>(c.epi, v, tc.q * BN + col, g.T, tc.p * kTileP, N,
+            swap_epilogue_store<IO>(c.epi, v, tc.q * BN + col, 0, g.T, tc.p * kTileP, N,
                                     [&](int t, int n0, uint4 piece) {
                                       *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
                                     });
@@ -136,15 +121,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       tc_fence_before();
-      if (threadIdx.x == 64) trace(432 + (n_units < 32 ? n_units : 31));
-      ++n_units;
       mbar_arrive(&c.acc_empty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
       }
     }
-    cluster_reduce_drain(g, c, red_seq);
   }
 
   tc_fence_before();
@@ -153,78 +135,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(*c.tmem_base, 2 * BN);
   }
-  pdl_wait();
-  if (threadIdx.x == 0) trace(1004);
-  if (g.csk <= 1 && g.sk_first < g.tiles) {
-    // Reduction phase: the grid finishes the shared stream-K tiles, summing
-    // the contributors' partials in order. Each thread owns 4 features of a
-    // (tile, token) row per step and keeps 4 steps of loads in flight.
-    uint32_t* bar = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(g.status) + 64);
-    const bool passed = grid_barrier_local(bar, bar + 16, g.status, g.wait_ns);
-    if (threadIdx.x == 0) trace(1002);
-    if (passed) {
-      const long long rows = static_cast<long long>(g.tiles - g.sk_first) * g.T;
-      const long long n4 = rows * 32;
-      const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
-      for (long long base = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; base < n4;
-           base += 4 * nthr) {
-        float4 a[4];
-        int tiles_[4], ts[4], f4[4], nc[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const long long i = base + k * nthr;
-          a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-          nc[k] = 0;
-          if (i >= n4) continue;
-          const long long rr = i >> 5;
-          tiles_[k] = g.sk_first + static_cast<int>(rr / g.T);
-          ts[k] = static_cast<int>(rr % g.T);
-          f4[k] = static_cast<int>(i & 31);
-          nc[k] = tile_contributors(g, tiles_[k]);
-        }
-        // Contributor-ordered sums; the loads of the 4 steps are independent.
-        for (int j = 0; j < g.max_contrib; ++j) {
-          bool any = false;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            if (j < nc[k]) {
-              any = true;
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                                          partial_tm<BN>(g, tiles_[k], j) + static_cast<size_t>(ts[k]) * kTileP) +
-                                      f4[k]);
-              a[k].x += v.x;
-              a[k].y += v.y;
-              a[k].z += v.z;
-              a[k].w += v.w;
-            }
-          }
-          if (!any) break;
-        }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          if (nc[k] < 2) continue;  // whole tiles were stored by their owner
-          const int n0 = (tiles_[k] % g.p_tiles) * kTileP + f4[k] * 4;
-          if (n0 >= g.N) continue;
-          if (bias != nullptr) {
-            a[k].x += io_to_f32<IO>(bias[n0]);
-            a[k].y += io_to_f32<IO>(bias[n0 + 1]);
-            a[k].z += io_to_f32<IO>(bias[n0 + 2]);
-            a[k].w += io_to_f32<IO>(bias[n0 + 3]);
-          }
-          IO h[4] = {f32_to_io<IO>(a[k].x), f32_to_io<IO>(a[k].y), f32_to_io<IO>(a[k].z),
-                     f32_to_io<IO>(a[k].w)};
-          *reinterpret_cast<uint2*>(y + static_cast<size_t>(ts[k]) * g.N + n0) = *reinterpret_cast<uint2*>(h);
-        }
-      }
-    }
-  }
   if (threadIdx.x == 0) trace(1001);
 }
 
 namespace {
 
 template <typename IO, int BN, bool SWAP>
-int launch_col(const GemmPlan& p0, const DeviceInfo& dev, const void* x, const void* w,
+int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
                const void* bias, void* y, int T, int N, int K, uint8_t* ws, size_t ws_bytes,
                cudaStream_t stream) {
   constexpr int STAGES = gemm_stages<BN>();
@@ -235,12 +152,8 @@ int launch_col(const GemmPlan& p0, const DeviceInfo& dev, const void* x, const v
     return set_error(PGB_ERR_UNSUPPORTED, "kernel needs %d B shared memory, device allows %d",
                      L::kBytes, dev.max_smem_optin);
   PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-  // Re-plan with the cluster sizes this kernel can actually co-schedule.
-  ClusterCaps caps;
-  query_cluster_caps(kern, kGemmThreads, L::kBytes, caps.max_active);
-  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, SIZE_MAX, false, &caps);
-  if (p.bn != p0.bn || p.swap != p0.swap)
-    return set_error(PGB_ERR_STATE, "col_gemm: inconsistent plan");
+  if (p.nsplit > 1 && split_recv_bytes(BN, p.nsplit) > static_cast<size_t>(STAGES) * L::kStageBytes)
+    return set_error(PGB_ERR_STATE, "col_gemm: split of %d does not fit the pipeline ring", p.nsplit);
   if (col_workspace_bytes(p) > ws_bytes)
     return set_error(PGB_ERR_INVALID, "col_gemm: workspace of %zu bytes, %zu needed", ws_bytes,
                      col_workspace_bytes(p));
@@ -263,25 +176,24 @@ int launch_col(const GemmPlan& p0, const DeviceInfo& dev, const void* x, const v
   g.q_tiles = p.q_tiles;
   g.tiles = p.tiles;
   g.dp_rounds = p.dp_rounds;
-  g.sk_first = p.sk_first;
+  g.split_first = p.split_first;
   g.grid = p.grid;
-  g.sk_grid = p.sk_grid;
-  g.max_contrib = p.max_contrib;
-  g.csk = p.csk;
-  g.n_clusters = p.n_clusters;
+  g.split_ctas = p.split_ctas;
+  g.nsplit = p.nsplit;
   g.status = reinterpret_cast<int*>(ws);
-  g.ws = reinterpret_cast<float*>(ws + kWsHeaderBytes);
+  g.ctr = reinterpret_cast<uint32_t*>(ws + kWsHeaderBytes);
+  g.xchg = reinterpret_cast<float*>(ws + kWsHeaderBytes + p.counter_bytes);
   g.wait_ns = 2000000000ull;  // 2 s: far beyond any legitimate pipeline stall
 
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(p.grid);  // n_clusters * csk for cluster split-K
+  cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   const CUtensorMap& ta = SWAP ? tm_w : tm_x;
   const CUtensorMap& tb = SWAP ? tm_x : tm_w;
-  // The reduction phase waits on every CTA: cooperative launch.
-  return launch_ex(cfg, /*cooperative=*/p.csk <= 1, p.csk, kern, ta, tb, g, static_cast<IO*>(y),
+  // The CTAs of a split tile wait for each other: cooperative launch.
+  return launch_ex(cfg, /*cooperative=*/p.split_ctas > 0, 1, kern, ta, tb, g, static_cast<IO*>(y),
                    static_cast<const IO*>(bias));
 }
 
@@ -418,10 +330,10 @@ extern "C" int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bi
   uint8_t* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  // The header (status word and grid-barrier counters) must start at zero;
-  // the partial slabs behind it are written before they are read.
+  // The status word and the split-tile counters must start at zero; the
+  // exchange area behind them is written before it is read.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  PGB_CUDA_TRY(cudaMemsetAsync(scratch, 0, kWsHeaderBytes, s));
+  PGB_CUDA_TRY(cudaMemsetAsync(scratch, 0, kWsHeaderBytes + p.counter_bytes, s));
   return pgb_col_gemm(x, w, bias, y, T, N, K, dtype, scratch, PGB_NOALLOC_SCRATCH_BYTES, stream);
 }
 

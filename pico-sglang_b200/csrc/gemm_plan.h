@@ -7,12 +7,6 @@
 
 namespace pgb {
 
-// Co-resident clusters of each size for one GEMM kernel configuration
-// (cudaOccupancyMaxActiveClusters); 0 = size not usable.
-struct ClusterCaps {
-  int max_active[9] = {};
-};
-
 struct GemmPlan {
   bool swap;      // true: MMA M side = output features (decode)
   int bn;         // MMA N (32, 64, 128 or 256)
@@ -20,36 +14,28 @@ struct GemmPlan {
   int p_tiles;
   int q_tiles;
   int tiles;      // p_tiles * q_tiles
-  int dp_rounds;  // whole tiles per CTA (round-robin part)
-  int sk_first;   // first stream-K tile (== tiles: none)
-  int grid;       // CTAs taking part in the GEMM
-  int sk_grid;    // CTAs taking part in the stream-K part (<= its k-blocks)
-  int max_contrib;        // partial slabs per stream-K tile
-  int csk;        // cluster split-K cluster size (0: not used)
-  int n_clusters; // clusters launched when csk > 1
-  size_t partial_bytes;   // partial scratch (0 without stream-K)
-  size_t counter_bytes;   // tile counters (aligned)
+  int dp_rounds;  // rounds of whole tiles [0, split_first), round-robin over `grid` CTAs
+  int split_first;  // first split tile (== tiles: none)
+  int grid;       // CTAs that take work (the launch may be wider)
+  int split_ctas; // CTAs [0, split_ctas) take one split segment after their whole tiles
+  int nsplit;     // k-ranges per split tile (1: no split tiles)
+  size_t exchange_bytes;  // split-K exchange area (0 without split tiles)
+  size_t counter_bytes;   // per-split-tile counters (aligned)
   double est_us;  // cost-model estimate of the chosen decomposition
 };
 
 // Plan y[T, N] = x[T, K] . W[N, K]^T on a device with `sms` SMs.
-//  - max_partial_bytes caps the stream-K scratch (SIZE_MAX: no cap);
-//  - all_streamk: the stream-K candidate covers every tile (the fused
-//    row-parallel kernel, whose decode phases read per-tile partials);
-//  - caps: cluster sizes usable for cluster split-K (nullptr: none);
-//  - fused_row: cost the candidates for the fused row-parallel kernel.
+// max_exchange_bytes caps the split-K exchange area (SIZE_MAX: no cap).
 // The cheapest candidate under a measured-rate cost model is returned.
-GemmPlan plan_gemm(int T, int N, int K, int sms, size_t max_partial_bytes, bool all_streamk = false,
-                   const ClusterCaps* caps = nullptr, bool fused_row = false);
+GemmPlan plan_gemm(int T, int N, int K, int sms, size_t max_exchange_bytes);
 
-// Cluster capacities measured on B200 (148 SMs, one CTA of ~216 KB shared
-// memory per SM), scaled to `sms`; used where no device can be queried.
-ClusterCaps nominal_cluster_caps(int sms);
-
-// Scratch layout used by the column GEMM: [status word | counters | partials].
+// Scratch layout used by the column GEMM: [status word, grid-barrier counters
+// | split-tile counters | exchange area]. The first
+// kWsHeaderBytes + counter_bytes bytes must be zero before the first call;
+// the kernel leaves them zero.
 constexpr size_t kWsHeaderBytes = 256;
 inline size_t col_workspace_bytes(const GemmPlan& p) {
-  return kWsHeaderBytes + p.counter_bytes + p.partial_bytes;
+  return kWsHeaderBytes + p.counter_bytes + p.exchange_bytes;
 }
 
 }  // namespace pgb

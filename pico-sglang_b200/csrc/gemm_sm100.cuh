@@ -22,9 +22,10 @@
 //                  128-row MMA side is always filled by weight rows and the
 //                  token side is only as wide as the batch.
 //
-// Shared tiles (stream-K, see GemmShape): a CTA that covers only part of a
-// tile's K range stores its f32 partial; after a grid barrier all warps sum
-// the partials of every shared tile in contributor order.
+// Split tiles (see GemmShape): the CTAs that share a tile's K range
+// reduce-scatter their f32 partials through L2 (split_reduce_tile); every
+// output element is summed in split order, so the result does not depend on
+// timing.
 #pragma once
 
 #include "sm100.cuh"
@@ -41,39 +42,28 @@ constexpr int kMaxRanks = 8;
 //
 // Work decomposition. The output is cut into tiles of 128 (P) x BN (Q); a
 // tile's reduction dimension is `kblocks` k-blocks of 64. Tiles
-// [0, sk_first) are whole tiles dealt round-robin: CTA c computes tiles
-// c, c + grid, ... (dp_rounds of them at most). Tiles [sk_first, tiles) are
-// stream-K tiles: their k-blocks are laid end to end and CTA c takes the
-// contiguous range [c*total/grid, (c+1)*total/grid) of them, cut at tile
-// boundaries into segments. With sk_first = dp_rounds * grid every CTA
-// streams the same number of k-blocks (+-1), so no SM idles while others
-// finish a last partial wave. A stream-K tile shared by several CTAs is
-// finished after a grid barrier (cooperative launch) by all warps together,
-// adding the contributors' f32 partials in contributor order, so the result
-// does not depend on timing.
-//
-// Cluster split-K (csk > 1) replaces both: the grid is made of clusters of
-// csk CTAs, cluster c computes tiles c, c + n_clusters, ..., and CTA r of the
-// cluster streams k-blocks [r*kblocks/csk, (r+1)*kblocks/csk) of each. The
-// csk partial accumulators are summed through distributed shared memory
-// (cluster_reduce_tile), so no partial leaves the chip.
+// [0, split_first) are whole tiles dealt round-robin: CTA c computes tiles
+// c, c + grid, ... (dp_rounds of them at most). Tiles [split_first, tiles)
+// are split tiles: split tile u is cut into nsplit equal k-ranges, and CTA
+// c < split_ctas takes k-range c % nsplit of split tile c / nsplit after its
+// whole tiles, so every SM streams about the same number of k-blocks and no
+// SM idles through a ragged last wave. The nsplit CTAs of a split tile are
+// co-resident (cooperative launch) and reduce-scatter their partials through
+// the exchange area (split_reduce_tile).
 struct GemmShape {
   int T, N, K;
   int kblocks;      // ceil(K / 64)
   int p_tiles;      // tiles along the MMA M side
   int q_tiles;      // tiles along the MMA N side
   int tiles;        // p_tiles * q_tiles
-  int dp_rounds;    // whole tiles per CTA before the stream-K part
-  int sk_first;     // first stream-K tile (== tiles: no stream-K part)
-  int grid;         // CTAs taking part in the round-robin part (<= gridDim.x)
-  int sk_grid;      // CTAs taking part in the stream-K part, <= grid and <=
-                    // its k-block count, so every stream-K range is non-empty
-  int max_contrib;  // partial slabs reserved per stream-K tile
-  int csk;          // > 1: cluster split-K with this cluster size (see SegIter)
-  int n_clusters;   // clusters in the launch when csk > 1
-  float* ws;        // partials [tiles - sk_first][max_contrib][BN tokens][128 features] f32
-  int* status;      // device status word (first error wins); the grid
-                    // barrier's counters follow it at +64 and +128 bytes
+  int dp_rounds;    // whole tiles per CTA at most
+  int split_first;  // first split tile (== tiles: none)
+  int grid;         // CTAs that take work (<= gridDim.x)
+  int split_ctas;   // (tiles - split_first) * nsplit
+  int nsplit;       // k-ranges per split tile
+  float* xchg;      // exchange area [tiles - split_first][nsplit][BN tokens][128 features] f32
+  uint32_t* ctr;    // per split tile: {published, finished} counters, zero at rest
+  int* status;      // device status word (first error wins)
   uint64_t wait_ns; // budget for every intra-kernel wait
 };
 
@@ -81,67 +71,26 @@ struct GemmShape {
 struct Seg {
   int tile, p, q;
   int kb0, kb1;   // k-block range [kb0, kb1)
-  int contrib;    // index of this CTA among the tile's contributors
-  int nctb;       // number of contributors (1 = this CTA owns the whole tile)
+  int contrib;    // index of this CTA among the tile's CTAs (its k-range)
+  int nctb;       // number of CTAs sharing the tile (1 = whole tile)
 };
 
-// CTA whose stream-K range contains stream-K k-block u.
-__host__ __device__ __forceinline__ int streamk_cta_of(long long u, long long total, int grid) {
-  return static_cast<int>(((u + 1) * grid - 1) / total);
-}
-
-__host__ __device__ __forceinline__ long long streamk_total(const GemmShape& g) {
-  return static_cast<long long>(g.tiles - g.sk_first) * g.kblocks;
-}
-
 // Iterates the segments of CTA `cta` in order: its whole tiles, then its
-// stream-K range. All roles of a CTA walk the same sequence. Host-callable
-// so the decomposition can be checked without a GPU.
+// split segment. All roles of a CTA walk the same sequence. Host-callable so
+// the decomposition can be checked without a GPU.
 struct SegIter {
-  long long u, u1, total;
-  int t, round, cta;
-  int ckb0, ckb1;  // cluster split-K: this CTA's k-range of every tile
+  int cta, round, split_done;
   __host__ __device__ __forceinline__ SegIter(const GemmShape& g, int cta_) {
     cta = cta_;
-    if (g.csk > 1) {
-      const int cl = cta / g.csk, r = cta % g.csk;
-      t = cl < g.n_clusters ? cl : g.tiles;
-      ckb0 = r * g.kblocks / g.csk;
-      ckb1 = (r + 1) * g.kblocks / g.csk;
-      round = 0;
-      u = u1 = total = 0;
-      return;
-    }
-    ckb0 = ckb1 = 0;
-    total = streamk_total(g);
-    round = 0;
-    t = cta;
-    if (cta < g.sk_grid && total > 0) {
-      u = total * cta / g.sk_grid;
-      u1 = total * (cta + 1) / g.sk_grid;
-    } else {  // no stream-K part, or a CTA beyond the stream-K grid
-      u = u1 = 0;
-    }
-    if (cta >= g.grid) round = g.dp_rounds;
+    round = cta < g.grid ? 0 : g.dp_rounds;
+    split_done = cta < g.split_ctas ? 0 : 1;
   }
   __device__ __forceinline__ explicit SegIter(const GemmShape& g) : SegIter(g, static_cast<int>(blockIdx.x)) {}
   __host__ __device__ __forceinline__ bool next(const GemmShape& g, Seg& s) {
-    if (g.csk > 1) {
-      if (t >= g.tiles) return false;
-      s.tile = t;
-      s.kb0 = ckb0;
-      s.kb1 = ckb1;
-      s.contrib = cta % g.csk;
-      s.nctb = g.csk;
-      s.p = t % g.p_tiles;
-      s.q = t / g.p_tiles;
-      t += g.n_clusters;
-      return true;
-    }
-    if (round < g.dp_rounds) {
-      s.tile = t + round * g.grid;
+    while (round < g.dp_rounds) {
+      s.tile = cta + round * g.grid;
       ++round;
-      if (s.tile < g.sk_first) {
+      if (s.tile < g.split_first) {
         s.kb0 = 0;
         s.kb1 = g.kblocks;
         s.contrib = 0;
@@ -152,23 +101,40 @@ struct SegIter {
       }
       round = g.dp_rounds;  // ragged last round: no more whole tiles
     }
-    if (u >= u1) return false;
-    const int rel = static_cast<int>(u / g.kblocks);
-    s.tile = g.sk_first + rel;
-    s.kb0 = static_cast<int>(u - static_cast<long long>(rel) * g.kblocks);
-    const long long rem = u1 - u;
-    s.kb1 = rem < static_cast<long long>(g.kblocks - s.kb0) ? s.kb0 + static_cast<int>(rem) : g.kblocks;
-    u += s.kb1 - s.kb0;
-    const long long first = static_cast<long long>(rel) * g.kblocks;
-    const int c0 = streamk_cta_of(first, total, g.sk_grid);
-    const int c1 = streamk_cta_of(first + g.kblocks - 1, total, g.sk_grid);
-    s.contrib = cta - c0;
-    s.nctb = c1 - c0 + 1;
+    if (split_done) return false;
+    split_done = 1;
+    const int S = g.nsplit, j = cta % S;
+    s.tile = g.split_first + cta / S;
+    s.kb0 = j * g.kblocks / S;
+    s.kb1 = (j + 1) * g.kblocks / S;
+    s.contrib = j;
+    s.nctb = S;
     s.p = s.tile % g.p_tiles;
     s.q = s.tile / g.p_tiles;
     return true;
   }
 };
+
+// Number of CTAs sharing `tile` (1 for whole tiles).
+__host__ __device__ __forceinline__ int tile_contributors(const GemmShape& g, int tile) {
+  return tile >= g.split_first ? g.nsplit : 1;
+}
+
+// Token columns [c0, c1) of a split tile (tile-relative, V real tokens) that
+// split r of S owns: runs of 4-token groups, cut evenly.
+__host__ __device__ __forceinline__ void split_cols(int V, int S, int r, int& c0, int& c1) {
+  const int G = (V + 3) >> 2;
+  c0 = (r * G / S) * 4;
+  c1 = ((r + 1) * G / S) * 4;
+  c0 = c0 < V ? c0 : V;
+  c1 = c1 < V ? c1 : V;
+}
+
+// Bytes of a split CTA's gather area in its ring: S slots (its own and the
+// others' pieces) of its largest column run, 128 f32 per column.
+__host__ __device__ constexpr size_t split_recv_bytes(int BN, int S) {
+  return static_cast<size_t>(S) * static_cast<size_t>((BN / 4 + S - 1) / S) * 4u * 128u * 4u;
+}
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -181,19 +147,21 @@ struct GemmSmem {
   static constexpr int kOffB = STAGES * kABytes;
   static constexpr int kOffEpi = kOffB + STAGES * kBBytes;
   static constexpr int kEpiBytes = 32 * kTileP * 2;  // 32 tokens x 128 features, 16-bit
-  static constexpr int kOffRed = kOffEpi + kEpiBytes;
-  static constexpr int kRedBytes = 32 * kTileP * 4;  // cluster split-K chunk: 32 tokens x 128 f32
-  static constexpr int kOffBar = kOffRed + kRedBytes;
-  static constexpr int kBarBytes = 8 * (2 * STAGES + 7) + 64;
+  static constexpr int kOffBar = kOffEpi + kEpiBytes;
+  static constexpr int kBarBytes = 8 * (2 * STAGES + 6) + 64;
   static constexpr int kBytes = kOffBar + kBarBytes + 1024;  // + alignment slack
 };
 
 // Pipeline depth that fills the shared-memory budget for a tile width.
+__host__ __device__ constexpr int gemm_stages_for(int bn) {
+  // 200 KB leaves room for the epilogue tile and the barriers.
+  return (200 * 1024) / (kTileP * kBlockK * 2 + bn * kBlockK * 2) > 12
+             ? 12
+             : (200 * 1024) / (kTileP * kBlockK * 2 + bn * kBlockK * 2);
+}
 template <int BN>
 constexpr int gemm_stages() {
-  constexpr int kBudget = 200 * 1024;  // leaves room for the epilogue tiles and barriers
-  constexpr int kStage = kTileP * kBlockK * 2 + BN * kBlockK * 2;
-  return kBudget / kStage > 12 ? 12 : kBudget / kStage;
+  return gemm_stages_for(BN);
 }
 
 struct GemmCtl {
@@ -208,9 +176,7 @@ struct GemmCtl {
   uint8_t* a;
   uint8_t* b;
   uint16_t* epi;  // [32][128] staging tile of the swap-orientation epilogue
-  float* red;     // [32][128] f32 chunk exchanged by cluster split-K
-  uint64_t* red_ready;  // all csk chunks of the cluster are written
-  uint64_t* red_free;   // all csk CTAs finished reading this CTA's chunk
+  uint64_t* xchg; // split tiles: the others' pieces have landed in the ring
 };
 
 template <int BN, int STAGES>
@@ -222,16 +188,14 @@ __device__ __forceinline__ GemmCtl gemm_carve_smem(uint8_t* raw) {
   c.a = base + L::kOffA;
   c.b = base + L::kOffB;
   c.epi = reinterpret_cast<uint16_t*>(base + L::kOffEpi);
-  c.red = reinterpret_cast<float*>(base + L::kOffRed);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::kOffBar);
   c.full = bars;
   c.empty = bars + STAGES;
   c.acc_full = bars + 2 * STAGES;
   c.acc_empty = bars + 2 * STAGES + 2;
   c.drain = bars + 2 * STAGES + 4;
-  c.red_ready = bars + 2 * STAGES + 5;
-  c.red_free = bars + 2 * STAGES + 6;
-  c.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
+  c.xchg = bars + 2 * STAGES + 5;
+  c.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
   c.abort = reinterpret_cast<int*>(c.tmem_base + 1);
   c.flag = c.abort + 1;
   return c;
@@ -463,183 +427,13 @@ __device__ __forceinline__ void epi_load_chunk(uint32_t tmem, int acc, int col, 
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// Number of CTAs contributing to `tile` (1 for whole tiles).
-__host__ __device__ __forceinline__ int tile_contributors(const GemmShape& g, int tile) {
-  if (g.csk > 1) return g.csk;
-  if (tile < g.sk_first) return 1;
-  const long long total = streamk_total(g);
-  const long long first = static_cast<long long>(tile - g.sk_first) * g.kblocks;
-  return streamk_cta_of(first + g.kblocks - 1, total, g.sk_grid) - streamk_cta_of(first, total, g.sk_grid) + 1;
-}
-
-// Token-major f32 partial of stream-K tile `tile`, contributor j, in swap
-// orientation: [BN tokens][128 features]. A warp stores 128 contiguous bytes
-// per token, and the reduction phase reads 8 consecutive features of a token
-// as two float4.
-template <int BN>
-__device__ __forceinline__ float* partial_tm(const GemmShape& g, int tile, int j) {
-  return g.ws + (static_cast<size_t>(tile - g.sk_first) * g.max_contrib + j) * BN * kTileP;
-}
-
-// Store this segment's accumulator (acc) as a token-major f32 partial.
-// Called by the 128 epilogue threads; tokens >= T are skipped.
-template <int BN>
-__device__ __forceinline__ void partial_store_tm(const GemmShape& g, const Seg& sg, uint32_t tmem,
-                                                 int acc) {
-  const int row = epi_row();
-  if (sg.contrib < 0 || sg.contrib >= g.max_contrib || sg.tile < g.sk_first) {
-    // Never store outside the reserved slabs; report instead.
-    if (row == 0) record_error(g.status, kDevBadArgs);
-    return;
-  }
-  float* dst = partial_tm<BN>(g, sg.tile, sg.contrib);
-#pragma unroll 1
-  for (int col = 0; col < BN; col += 32) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, col), r);
-    tmem_ld_wait();
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const int t = sg.q * BN + col + j;
-      if (t < g.T) __stcg(dst + static_cast<size_t>(col + j) * kTileP + row, __uint_as_float(r[j]));
-    }
-  }
-}
-
-// Grid-wide barrier for a cooperative launch on one GPU. arrive/gen live in
-// global memory and are zero at rest; the last CTA to arrive resets the
-// counter and bumps the generation. Bounded: returns false (and records an
-// error) when the wait runs out or another CTA already failed.
-__device__ __forceinline__ bool grid_barrier_local(uint32_t* arrive, uint32_t* gen, int* status,
-                                                   uint64_t wait_ns) {
-  __shared__ int s_ok;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    const uint32_t g0 = ld_acquire_gpu(gen);
-    __threadfence();
-    const uint32_t old = atom_add_acqrel_gpu(arrive, 1u);
-    if (old == gridDim.x - 1) {
-      *arrive = 0u;
-      __threadfence();
-      st_release_gpu(gen, g0 + 1u);
-    } else {
-      Deadline d(wait_ns);
-      volatile int* st = status;
-      while (ld_acquire_gpu(gen) == g0) {
-        if (d.expired()) {
-          record_error(status, kDevTimeoutGrid);
-          ok = 0;
-          break;
-        }
-        if ((d.n & 255u) == 0u && *st != 0) {
-          ok = 0;
-          break;
-        }
-      }
-    }
-    s_ok = ok;
-  }
-  __syncthreads();
-  return s_ok != 0;
-}
-
-// Cluster split-K reduction of one tile (swap orientation). Every one of the
-// 128 epilogue threads of every CTA of the cluster calls this for the same
-// tile, with its own partial accumulator `acc`. Per 32-token chunk: each CTA
-// writes its partial to its shared `red` buffer (token-major), signals the
-// cluster, then reduces its share of the feature groups over the csk buffers
-// in CTA-rank order through DSMEM and hands every finished 4-feature piece to
-// emit(t, n0, float4), then signals that it is done reading. `seq` counts
-// chunks across tiles (mbarrier parities). Only the epilogue warps take part,
-// so the producer and MMA warps keep streaming the next tile meanwhile.
-template <int BN, typename Emit4>
-__device__ __forceinline__ bool cluster_reduce_tile(const GemmShape& g, const Seg& sg, const GemmCtl& c,
-                                                    uint32_t tmem, int acc, uint32_t& seq, Emit4&& emit) {
-  const int C = g.csk;
-  const int rank = static_cast<int>(blockIdx.x) % C;
-  const int row = epi_row();
-  const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
-  const int g0 = rank * (kTileP / 4) / C, g1 = (rank + 1) * (kTileP / 4) / C;
-  const int ng = g1 - g0;
-  bool ok = true;
-#pragma unroll 1
-  for (int col = 0; col < BN; col += 32) {
-    if (seq > 0 && !mbar_wait_cluster(c.red_free, (seq - 1) & 1u, g.wait_ns)) ok = false;
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, col), r);
-    tmem_ld_wait();
-#pragma unroll
-    for (int j = 0; j < 32; ++j) c.red[j * kTileP + row] = __uint_as_float(r[j]);
-    named_bar_sync(1, kEpiThreads);
-    // One thread per destination CTA arrives, so the C release-arrives are in
-    // flight together; each releases at cluster scope, and the named barrier
-    // above orders every thread's buffer writes before it.
-    if (tid == 0) trace(1010);
-    if (tid < C) mbar_arrive_cluster(dsmem_addr(c.red_ready, tid));
-    if (tid == 0) trace(1011);
-    if (!mbar_wait_cluster(c.red_ready, seq & 1u, g.wait_ns)) ok = false;
-    if (tid == 0) trace(1012);
-    if (ok) {
-      const int items = 32 * ng;
-      for (int it0 = tid; it0 < items; it0 += 2 * kEpiThreads) {
-        // Two items per pass: all 2*C DSMEM loads in flight before the adds.
-        float4 v[2][8];
-        int jj[2], gg[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int it = it0 + k * kEpiThreads;
-          jj[k] = it < items ? it / ng : -1;
-          gg[k] = it < items ? g0 + it % ng : 0;
-          if (jj[k] >= 0) {
-            const float* my = c.red + jj[k] * kTileP + gg[k] * 4;
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              if (q < C) v[k][q] = ld_dsmem_f4(dsmem_addr(my, q));
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          if (jj[k] < 0) continue;
-          float4 a = v[k][0];
-#pragma unroll
-          for (int q = 1; q < 8; ++q) {
-            if (q < C) {
-              a.x += v[k][q].x;
-              a.y += v[k][q].y;
-              a.z += v[k][q].z;
-              a.w += v[k][q].w;
-            }
-          }
-          const int t = sg.q * BN + col + jj[k], n0 = sg.p * kTileP + gg[k] * 4;
-          if (t < g.T && n0 < g.N) emit(t, n0, a);
-        }
-      }
-    }
-    named_bar_sync(1, kEpiThreads);
-    if (tid == 0) trace(1013);
-    if (tid < C) mbar_arrive_cluster(dsmem_addr(c.red_free, tid));
-    ++seq;
-  }
-  if (!ok) record_error(g.status, kDevTimeoutPipeline);
-  return ok;
-}
-
-// Before a CTA of a split-K cluster retires, every CTA of the cluster must
-// have finished reading its reduction buffer.
-__device__ __forceinline__ void cluster_reduce_drain(const GemmShape& g, const GemmCtl& c, uint32_t seq) {
-  if (g.csk > 1 && seq > 0 && !mbar_wait_cluster(c.red_free, (seq - 1) & 1u, g.wait_ns))
-    record_error(g.status, kDevTimeoutPipeline);
-  if (threadIdx.x == kGemmThreads - kEpiThreads) trace(1014);
-}
-
 // Swap orientation: this thread holds v[j] = out(feature p*128 + row,
 // token t0 + j), j < 32. Stage the 32 x 128 block through shared memory so
 // it leaves as 16-byte pieces of token rows. emit(t, n0, piece) receives
-// 8 consecutive features [n0, n0 + 8) of token t. All 128 epilogue threads
-// call this together.
+// 8 consecutive features [n0, n0 + 8) of token t, for tokens in
+// [t_lo, t_hi). All 128 epilogue threads call this together.
 template <typename IO, typename Emit>
-__device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* v, int t0, int T,
+__device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* v, int t0, int t_lo, int t_hi,
                                                     int n_base, int N, Emit&& emit) {
   const int row = epi_row();
   named_bar_sync(1, kEpiThreads);  // previous chunk fully read
@@ -655,8 +449,147 @@ __device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* 
     const int idx = tid + k * kEpiThreads;  // 512 pieces: 32 tokens x 16 pieces
     const int j = idx >> 4, piece = idx & 15;
     const int t = t0 + j, n0 = n_base + piece * 8;
-    if (t < T && n0 < N) emit(t, n0, *reinterpret_cast<const uint4*>(epi + j * kTileP + piece * 8));
+    if (t >= t_lo && t < t_hi && n0 < N) emit(t, n0, *reinterpret_cast<const uint4*>(epi + j * kTileP + piece * 8));
   }
+}
+
+// Split tile (swap orientation), called by the 128 epilogue threads of each
+// of the tile's nsplit CTAs with its partial accumulator `acc` over its own
+// k-range. The tile's real token columns are cut into nsplit runs
+// (split_cols), one per CTA. Each CTA
+//   1. stores its partial for the columns the other CTAs own into its slab of
+//      the exchange area (token-major f32: a warp writes 128 contiguous bytes
+//      per token) and publishes it with one release on the tile's counter;
+//   2. once all nsplit CTAs have published, bulk-copies (cp.async.bulk, off
+//      the load/store unit) the others' pieces of its own columns into its
+//      pipeline ring, which is idle after its last MMA;
+//   3. sums its columns in split order (its own values were parked in its
+//      ring in step 1), adds the bias once, rounds and hands 16-byte pieces
+//      of token rows to emit(t, n0, uint4) through the shared staging tile;
+//   4. bumps the tile's second counter; the last CTA to finish resets both,
+//      so the counters are zero again for the next launch.
+// Returns false (and records an error) if a wait runs out.
+template <typename IO, int BN, typename Emit16>
+__device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg& sg, const GemmCtl& c, uint32_t tmem,
+                                                  int acc, const IO* bias, Emit16&& emit) {
+  const int S = sg.nctb, j = sg.contrib, u = sg.tile - g.split_first;
+  const int row = epi_row();
+  const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
+  const int t_base = sg.q * BN;
+  const int V = min(BN, g.T - t_base);
+  const size_t slab = static_cast<size_t>(BN) * kTileP;
+  uint32_t* ctr = g.ctr + 2 * u;
+  int my0, my1;
+  split_cols(V, S, j, my0, my1);
+  bool ok = true;
+
+  // 1. This CTA's partial: the other CTAs' columns to its exchange slab, its
+  //    own columns to slot j of the gather area in its ring (idle after the
+  //    last MMA), laid out [S][n_mine][128] f32.
+  const int n_mine = my1 - my0;
+  float* recv = reinterpret_cast<float*>(c.a);
+  float* mine = g.xchg + static_cast<size_t>(u * S + j) * slab;
+  float* own = recv + static_cast<size_t>(j) * n_mine * kTileP + row;
+#pragma unroll 1
+  for (int cb = 0; cb < V; cb += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, cb), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      const int col = cb + jj;
+      const float x = __uint_as_float(r[jj]);
+      const bool is_mine = col >= my0 && col < my1;
+      if (is_mine) own[static_cast<size_t>(col - my0) * kTileP] = x;
+      if (!is_mine && col < V) __stcg(mine + static_cast<size_t>(col) * kTileP + row, x);
+    }
+  }
+  // bar.sync, then one gpu-scope release: every thread's stores are ordered
+  // before the publication.
+  named_bar_sync(1, kEpiThreads);
+  if (tid == 0) {
+    atom_add_acqrel_gpu(ctr, 1u);
+    trace(1011);
+  }
+
+  // 2. Gather the other CTAs' pieces of this CTA's columns into their slots.
+  if (n_mine > 0) {
+    if (tid == 0) {
+      int okw = 1;
+      Deadline d(g.wait_ns);
+      volatile int* st = g.status;
+      while (ld_acquire_gpu(ctr) < static_cast<uint32_t>(S)) {
+        if (d.expired()) {
+          record_error(g.status, kDevTimeoutGrid);
+          okw = 0;
+          break;
+        }
+        if ((d.n & 255u) == 0u && *st != 0) {
+          okw = 0;
+          break;
+        }
+      }
+      if (okw) {
+        fence_proxy_async_global();  // the bulk copies read what the acquire made visible
+        const uint32_t piece = static_cast<uint32_t>(n_mine) * kTileP * 4u;
+        mbar_arrive_expect_tx(c.xchg, piece * static_cast<uint32_t>(S - 1));
+        for (int q = 0; q < S; ++q) {
+          if (q == j) continue;
+          bulk_g2s(recv + static_cast<size_t>(q) * n_mine * kTileP,
+                   g.xchg + static_cast<size_t>(u * S + q) * slab + static_cast<size_t>(my0) * kTileP, piece, c.xchg);
+        }
+        if (!mbar_wait(c.xchg, 0u, g.wait_ns, nullptr)) {
+          record_error(g.status, kDevTimeoutPipeline);
+          okw = 0;
+        }
+      }
+      *c.flag = okw;
+      trace(1012);
+    }
+    named_bar_sync(1, kEpiThreads);
+    ok = *reinterpret_cast<volatile int*>(c.flag) != 0;
+  }
+
+  // 3. Sum the S slots in split order, add the bias, round, store. Shared
+  //    memory only and branch-free: token indices past this CTA's run are
+  //    clamped (those lanes of the staging tile are not emitted).
+  if (ok && n_mine > 0) {
+    const int nf = sg.p * kTileP + row;
+    const float b = (bias != nullptr && nf < g.N) ? io_to_f32<IO>(bias[nf]) : 0.f;
+    const float* base = recv + row;
+#pragma unroll 1
+    for (int c0 = 0; c0 < n_mine; c0 += 32) {
+      if (tid == 0 && c0 == 0) trace(1014);
+      const int lim = n_mine - 1 - c0;
+      float v[32];
+      const float* s0 = base + static_cast<size_t>(c0) * kTileP;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) v[jj] = s0[static_cast<size_t>(min(jj, lim)) * kTileP];
+#pragma unroll 1
+      for (int q = 1; q < S; ++q) {
+        const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) v[jj] += sq[static_cast<size_t>(min(jj, lim)) * kTileP];
+      }
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) v[jj] += b;
+      if (tid == 0 && c0 == 0) trace(1015);
+      swap_epilogue_store<IO>(c.epi, v, t_base + my0 + c0, t_base + my0, t_base + my1, sg.p * kTileP, g.N, emit);
+      if (tid == 0 && c0 == 0) trace(1016);
+    }
+  }
+
+  // 4. The last CTA of the tile to finish resets its counters.
+  named_bar_sync(1, kEpiThreads);
+  if (tid == 0) {
+    trace(1013);
+    const uint32_t old = atom_add_acqrel_gpu(ctr + 1, 1u);
+    if (old == static_cast<uint32_t>(S) - 1u) {
+      ctr[0] = 0u;
+      ctr[1] = 0u;
+    }
+  }
+  return ok;
 }
 
 }  // namespace pgb

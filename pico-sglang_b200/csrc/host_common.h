@@ -9,10 +9,8 @@
 
 #include <cstdarg>
 #include <cstdio>
-#include <map>
 #include <mutex>
 #include <string>
-#include <utility>
 
 #include "../../include/pgb.h"
 
@@ -49,42 +47,6 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // Whether launches request programmatic stream serialization (PDL). Cleared
 // for the process if the driver refuses a launch with it.
 bool& pdl_enabled();
-
-// Co-resident clusters of size 2..8 for kernel `kern` launched with
-// `threads` threads and `smem` bytes of dynamic shared memory on the current
-// device (0 where a size is not usable). Cached per (device, kernel, smem).
-template <typename Kern>
-void query_cluster_caps(Kern kern, int threads, int smem, int* max_active /* [9] */) {
-  static std::mutex mu;
-  static std::map<std::pair<std::pair<int, const void*>, int>, std::pair<int, int[9]>> cache;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const auto key = std::make_pair(std::make_pair(dev, reinterpret_cast<const void*>(kern)), smem);
-  std::lock_guard<std::mutex> lk(mu);
-  auto it = cache.find(key);
-  if (it == cache.end()) {
-    std::pair<int, int[9]> v{};
-    for (int C = 0; C <= 8; ++C) v.second[C] = 0;
-    for (int C : {2, 3, 4, 6, 8}) {
-      cudaLaunchConfig_t cfg{};
-      cfg.gridDim = dim3(C);
-      cfg.blockDim = dim3(threads);
-      cfg.dynamicSmemBytes = smem;
-      cudaLaunchAttribute at[1];
-      at[0].id = cudaLaunchAttributeClusterDimension;
-      at[0].val.clusterDim.x = C;
-      at[0].val.clusterDim.y = 1;
-      at[0].val.clusterDim.z = 1;
-      cfg.attrs = at;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess) v.second[C] = n;
-      else (void)cudaGetLastError();
-    }
-    it = cache.emplace(key, v).first;
-  }
-  for (int C = 0; C <= 8; ++C) max_active[C] = it->second.second[C];
-}
 
 // Launch with cudaLaunchKernelEx: optional cooperative attribute, cluster
 // dimension (cluster > 1) and PDL. If the PDL combination is refused,

@@ -5,6 +5,8 @@
 // because CTAs wait on the arrival of every other CTA of the grid.
 #pragma once
 
+#include <type_traits>
+
 #include "comm.h"
 #include "sm100.cuh"
 
@@ -25,16 +27,15 @@ __device__ __forceinline__ uint32_t comm_begin(const CommDev& cm) {
 // early when another CTA already recorded an error. Every CTA must call this
 // with the same `bar` sequence, errors or not, so counters stay balanced.
 // sys_scope = false (one GPU) only synchronises the grid, at device scope.
-__device__ __forceinline__ bool grid_cross_barrier(const CommDev& cm, int bar, uint32_t e,
+static __device__ __noinline__ bool grid_cross_barrier(const CommDev& cm, int bar, uint32_t e,
                                                    bool sys_scope) {
   __shared__ int s_ok;
   __syncthreads();
   if (threadIdx.x == 0) {
     int ok = 1;
-    if (sys_scope)
-      __threadfence_system();
-    else
-      __threadfence();
+    // bar.sync above, then a gpu-scope release: the CTA's writes (local and
+    // peer memory) are ordered before its arrival, and the last CTA acquires
+    // them all before it publishes the flag (system scope across GPUs).
     const uint32_t old = atom_add_acqrel_gpu(&cm.arrive[bar], 1u);
     if (old == gridDim.x - 1) {
       cm.arrive[bar] = 0u;
@@ -74,7 +75,6 @@ __device__ __forceinline__ bool grid_cross_barrier(const CommDev& cm, int bar, u
 __device__ __forceinline__ void comm_end(const CommDev& cm, uint32_t e) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     const uint32_t old = atom_add_acqrel_gpu(&cm.arrive[kBarFinish], 1u);
     if (old == gridDim.x - 1) {
       cm.arrive[kBarFinish] = 0u;
@@ -192,91 +192,117 @@ __device__ __forceinline__ float block_sum(float v, float* red /* >= 32 floats *
   return t;
 }
 
-// Phase 2 for one row t: obtain the f32 sum of row t's sources for every
-// 8-feature vector from sum8(t, n0, float[8]), round it to the I/O type (the
-// reference materialises the reduced tensor in that type), then either write
-// it (do_norm == 0) or residual-add + RMSNorm it. Writes out[t] and
-// residual[t] locally and, for two-shot, pushes both rows to every peer's
-// result region. MAXV bounds the 8-element vectors per thread.
-template <typename IO, int MAXV, typename Sum8>
-__device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity,
-                                           int t, int width, IO* out, IO* residual,
-                                           const IO* norm_w, float eps, int do_norm, float* red,
-                                           Sum8&& sum8) {
-  const int nvec = width >> 3;
-  float s[MAXV][8];
-  float ss = 0.f;
+// Unpack 8 IO values held in 16 bytes.
+template <typename IO>
+__device__ __forceinline__ void unpack8_io(const uint4& u, float* v) {
+  if constexpr (std::is_same<IO, __nv_bfloat16>::value) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int v = threadIdx.x + i * blockDim.x;
-    if (v < nvec) {
-      sum8(t, v * 8, s[i]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) s[i][j] = round_io<IO>(s[i][j]);
-      if (do_norm) {
-        float r[8];
-        load8<IO>(residual + static_cast<size_t>(t) * width + v * 8, r);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          s[i][j] += r[j];
-          ss += s[i][j] * s[i][j];
-        }
-      }
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = __uint_as_float(w[j] << 16);
+      v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
     }
-  }
-  float rcp = 1.f;
-  if (do_norm) rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
-  const bool push = !rs.oneshot && cm.world > 1;
+  } else {
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
-    const int v = threadIdx.x + i * blockDim.x;
-    if (v < nvec) {
-      const size_t off = static_cast<size_t>(t) * width + v * 8;
-      float o[8];
-      if (do_norm) {
-        float w[8];
-        load8<IO>(norm_w + v * 8, w);
-        store8<IO>(residual + off, s[i]);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = s[i][j] * rcp * w[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = s[i][j];
-      }
-      store8<IO>(out + off, o);
-      if (push) {
-        for (int d = 0; d < cm.world; ++d) {
-          if (d == cm.rank) continue;
-          uint8_t* base = cm.results[d] + parity * cm.result_parity_bytes;
-          store8<IO>(reinterpret_cast<IO*>(base) + off, o);
-          if (do_norm) store8<IO>(reinterpret_cast<IO*>(base + cm.result_parity_bytes / 2) + off, s[i]);
-        }
-      }
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
     }
   }
 }
 
-// Sum over the ranks' partial rows pushed into this rank's slot region.
-template <typename SlotT>
-struct SlotSum8 {
-  const CommDev& cm;
-  const RowSplit& rs;
-  uint32_t parity;
-  int width;
-  __device__ __forceinline__ void operator()(int t, int n0, float* out) const {
-    const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
-    const SlotT* slot0 = reinterpret_cast<const SlotT*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes);
-    const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
+// Phase 2 for one row t. The row's sources are the world slot rows this rank
+// received (one per source rank, already summed over k-ranges and rounded to
+// IO); their sum is rounded to IO (the reference materialises the reduced
+// tensor in that type) and then either written (do_norm == 0) or
+// residual-added and RMS-normalised. Writes out[t] and residual[t] locally
+// and, for two-shot, pushes both rows to every peer's result region.
+//
+// This code runs once per launch, after the weight stream has displaced it
+// from the caches, so its instruction footprint costs more than its memory
+// round trips: the loops stay rolled. Each step requests the source, residual
+// and norm-weight vectors together; the f32 pre-norm row and the weights wait
+// in shared memory `srow` (width f32 + width IO values) for the second pass,
+// which only reads shared memory and stores. IO is 16-bit.
+template <typename IO, int MAXV>
+__device__ __noinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity, int t, int width,
+                                        IO* out, IO* residual, const IO* norm_w, float eps, int do_norm, float* red,
+                                        float* srow) {
+  static_assert(sizeof(IO) == 2, "16-bit I/O");
+  const int nvec = width >> 3;
+  const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
+  const IO* slot0 = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes) +
+                    static_cast<size_t>(lr) * width;
+  const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
+  uint4* wrow = reinterpret_cast<uint4*>(srow + width);
+  const size_t row_off = static_cast<size_t>(t) * width;
+  float ss = 0.f;
+#pragma unroll 1
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    uint4 rr = make_uint4(0u, 0u, 0u, 0u), wv = rr;
+    if (do_norm) {
+      rr = __ldcg(reinterpret_cast<const uint4*>(residual + row_off) + v);
+      wv = __ldg(reinterpret_cast<const uint4*>(norm_w) + v);
+    }
+    float s8[8], p[8];
+    unpack8_io<IO>(__ldcg(reinterpret_cast<const uint4*>(slot0) + v), s8);
+#pragma unroll 1
+    for (int d = 1; d < cm.world; ++d) {
+      unpack8_io<IO>(__ldcg(reinterpret_cast<const uint4*>(slot0 + d * src_stride) + v), p);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) out[j] = 0.f;
-    for (int src = 0; src < cm.world; ++src) {
-      float p[8];
-      load8<SlotT>(slot0 + src * src_stride + static_cast<size_t>(lr) * width + n0, p);
+      for (int j = 0; j < 8; ++j) s8[j] += p[j];
+    }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) out[j] += p[j];
+    for (int j = 0; j < 8; ++j) s8[j] = round_io<IO>(s8[j]);
+    if (do_norm) {
+      unpack8_io<IO>(rr, p);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        s8[j] += p[j];
+        ss += s8[j] * s8[j];
+      }
+      wrow[v] = wv;
+    }
+    float4* dst = reinterpret_cast<float4*>(srow) + 2 * v;
+    dst[0] = make_float4(s8[0], s8[1], s8[2], s8[3]);
+    dst[1] = make_float4(s8[4], s8[5], s8[6], s8[7]);
+  }
+  float rcp = 1.f;
+  if (do_norm) rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
+  else __syncthreads();
+  const bool push = !rs.oneshot && cm.world > 1;
+#pragma unroll 1
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(srow)[2 * v];
+    const float4 b = reinterpret_cast<const float4*>(srow)[2 * v + 1];
+    float s8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float o[8];
+    if (do_norm) {
+      float w[8];
+      unpack8_io<IO>(wrow[v], w);
+      store8<IO>(residual + row_off + v * 8, s8);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = s8[j] * rcp * w[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = s8[j];
+    }
+    store8<IO>(out + row_off + v * 8, o);
+    if (push) {
+#pragma unroll 1
+      for (int d = 0; d < cm.world; ++d) {
+        if (d == cm.rank) continue;
+        uint8_t* base = cm.results[d] + parity * cm.result_parity_bytes;
+        store8<IO>(reinterpret_cast<IO*>(base) + row_off + v * 8, o);
+        if (do_norm) store8<IO>(reinterpret_cast<IO*>(base + cm.result_parity_bytes / 2) + row_off + v * 8, s8);
+      }
     }
   }
-};
+  // srow is reused by the next row of this CTA.
+  __syncthreads();
+}
 
 // Phase 3 (two-shot): copy the rows owned by other ranks from this rank's
 // result region into out / residual.

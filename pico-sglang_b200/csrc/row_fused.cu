@@ -6,9 +6,9 @@
 //   -> all_reduce(y, "sum")     memcpy + ncclAllReduce + memcpy        (csrc/src/pynccl.cu:95-137)
 //   -> RMSNormFused.forward     flashinfer fused_add_rmsnorm           (layers/norm.py:73-75)
 //
-// Phase 1 (tcgen05 GEMM, persistent): each finished output tile (split-K
-//   combined on this GPU) is rounded to the I/O type and stored straight
-//   from registers into the slot region of the rank(s) that reduce its rows:
+// Phase 1 (tcgen05 GEMM, persistent): each finished output tile (split
+//   tiles reduce-scattered between their CTAs on this GPU) is rounded to the
+//   I/O type and stored into the slot region of the rank(s) that reduce its rows:
 //   every rank for one-shot, the row owner for two-shot. Remote stores go
 //   over NVLink while later tiles are still being multiplied.
 // Barrier 0: grid arrival, then a release flag to every rank, then bounded
@@ -38,7 +38,6 @@ struct RowArgs {
   const void* bias;
   float eps;
   int do_norm;
-  uint32_t* grid_bar;  // local grid barrier counters (arrive, generation at +64 B)
 };
 
 template <typename IO>
@@ -146,8 +145,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init(&c.acc_empty[0], kEpiThreads);
     mbar_init(&c.acc_empty[1], kEpiThreads);
     mbar_init(c.drain, 1);
-    mbar_init(c.red_ready, g.csk > 1 ? g.csk : 1);
-    mbar_init(c.red_free, g.csk > 1 ? g.csk : 1);
+    mbar_init(c.xchg, 1);
     *c.abort = 0;
     fence_mbar_init();
     trace(1005);
@@ -162,11 +160,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (g.csk > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   if (threadIdx.x == 0) pdl_launch_dependents();
-  // Decode plans put every tile in the stream-K part; their segments leave
-  // f32 partials that the reduction phases combine.
-  const bool staged = g.csk <= 1 && g.sk_first == 0 && g.tiles > 0;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -189,7 +183,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row = epi_row();
     const IO* bias = static_cast<const IO*>(a.bias);
     (void)row;
-    uint32_t red_seq = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     SegIter it(g);
@@ -201,26 +194,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after();
-      if (g.csk > 1) {
-        // Cluster split-K: sum the cluster's partials on chip, round to the
-        // I/O type and store into the slots of the reducing rank(s).
-        cluster_reduce_tile<BN>(g, tc, c, tmem, acc, red_seq, [&](int t, int n0, float4 v) {
-          if (bias != nullptr) {
-            v.x += io_to_f32<IO>(bias[n0]);
-            v.y += io_to_f32<IO>(bias[n0 + 1]);
-            v.z += io_to_f32<IO>(bias[n0 + 2]);
-            v.w += io_to_f32<IO>(bias[n0 + 3]);
-          }
-          IO h[4] = {f32_to_io<IO>(v.x), f32_to_io<IO>(v.y), f32_to_io<IO>(v.z), f32_to_io<IO>(v.w)};
-          row_store4<IO>(a, parity, t, n0, *reinterpret_cast<uint2*>(h));
+      if (tc.nctb > 1) {
+        // Split tile: reduce-scatter with the tile's other CTAs through L2,
+        // then store into the slots of the reducing rank(s).
+        split_reduce_tile<IO, BN>(g, tc, c, tmem, acc, bias, [&](int t, int n0, uint4 piece) {
+          row_store_piece<IO>(a, parity, t, n0, piece);
         });
-      } else if (staged) {
-        // Decode: every segment leaves an f32 token-major partial; the
-        // reduction phases below combine contributors, ranks and residual.
-        partial_store_tm<BN>(g, tc, tmem, acc);
       } else {
-        // Whole tiles (prefill): round and store straight into the slots of
-        // the rank(s) that reduce these rows.
+        // Whole tiles: round and store straight into the slots of the
+        // rank(s) that reduce these rows.
 #pragma unroll 1
         for (int col = 0; col < BN; col += 32) {
           float v[32];
@@ -232,7 +214,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += b;
             }
-            swap_epilogue_store<IO>(c.epi, v, tc.q * BN + col, g.T, tc.p * kTileP, g.N,
+            swap_epilogue_store<IO>(c.epi, v, tc.q * BN + col, 0, g.T, tc.p * kTileP, g.N,
                                     [&](int t, int n0, uint4 piece) {
                                       row_store_piece<IO>(a, parity, t, n0, piece);
                                     });
@@ -262,7 +244,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         acc_phase ^= 1u;
       }
     }
-    cluster_reduce_drain(g, c, red_seq);
   }
 
   tc_fence_before();
@@ -279,77 +260,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   IO* out = static_cast<IO*>(a.out);
   IO* residual = static_cast<IO*>(a.residual);
   const IO* norm_w = static_cast<const IO*>(a.norm_w);
-  const IO* bias = static_cast<const IO*>(a.bias);
-  // Sum of the contributors' f32 partials (plus the bias once) for
-  // features [n0, n0 + 8) of token t; swap orientation, so the tile is
-  // n0 / 128 and the partial row is token-major.
-  auto slab_sum8 = [&](int t, int n0, float* o) {
-    const int tile = n0 / kTileP;
-    const int n = tile_contributors(g, tile);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = 0.f;
-    const float* base = partial_tm<BN>(g, tile, 0) + static_cast<size_t>(t) * kTileP + (n0 % kTileP);
-    const size_t slab = static_cast<size_t>(BN) * kTileP;
-    // Batches of up to 8 contributors: all loads of a batch in flight
-    // before the first add; the adds stay in contributor order.
-    for (int j0 = 0; j0 < n; j0 += 8) {
-      float4 lo[8], hi[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (j0 + k < n) {
-          const float4* src = reinterpret_cast<const float4*>(base + (j0 + k) * slab);
-          lo[k] = __ldcg(src);
-          hi[k] = __ldcg(src + 1);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (j0 + k < n) {
-          o[0] += lo[k].x; o[1] += lo[k].y; o[2] += lo[k].z; o[3] += lo[k].w;
-          o[4] += hi[k].x; o[5] += hi[k].y; o[6] += hi[k].z; o[7] += hi[k].w;
-        }
-      }
-    }
-    if (bias != nullptr) {
-      float b[8];
-      load8<IO>(bias + n0, b);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) o[q] += b[q];
-    }
-  };
-
-  bool ok = true;
-  if (staged && multi) {
-    // Phase 1.5: combine this rank's contributors, round to the I/O type and
-    // push each 8-feature piece to the rank(s) that reduce its row.
-    uint32_t* gb = a.grid_bar;
-    ok = grid_barrier_local(gb, gb + 16, g.status, g.wait_ns);
-    if (ok) {
-      const int nvec = g.N >> 3;
-      const long long items = static_cast<long long>(g.T) * nvec;
-      for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < items;
-           i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int t = static_cast<int>(i / nvec), n0 = static_cast<int>(i % nvec) * 8;
-        float v[8];
-        slab_sum8(t, n0, v);
-        row_store_piece<IO>(a, parity, t, n0, pack8<IO>(v));
-      }
-    }
-  }
   // A failure anywhere on this GPU poisons the status; the barriers then
   // stop waiting and the later phases are skipped.
   if (threadIdx.x == 0) trace(1004);
-  const bool ok0 = grid_cross_barrier(a.cm, kBarPartials, e, multi) && ok;
+  const bool ok0 = grid_cross_barrier(a.cm, kBarPartials, e, multi);
   if (threadIdx.x == 0) trace(1002);
   if (ok0) {
     const int r0 = a.rs.first(a.cm.rank), r1 = a.rs.last(a.cm.rank);
-    for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x) {
-      if (staged && !multi)
-        reduce_row<IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps,
-                                   a.do_norm, s_red, slab_sum8);
-      else
-        reduce_row<IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps,
-                                   a.do_norm, s_red, SlotSum8<IO>{a.cm, a.rs, parity, g.N});
+    // The pipeline ring is idle from here on: it holds the f32 pre-norm row.
+    float* srow = reinterpret_cast<float*>(c.a);
+    int nrow = 0;
+    for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x, ++nrow) {
+      reduce_row<IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps, a.do_norm, s_red,
+                                 srow);
+      if (threadIdx.x == 0 && nrow < 3) trace(1017 + nrow);
     }
   }
   if (multi && !a.rs.oneshot) {
@@ -368,22 +292,12 @@ int launch_row(pgb_comm* c, RowArgs args, const void* x, const void* w, cudaStre
   constexpr int STAGES = gemm_stages<BN>();
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kBytes + 256 <= 232448, "shared memory budget");
+  static_assert(static_cast<size_t>(STAGES) * L::kStageBytes >= kGemmThreads * 8 * kRowMaxVec * (4 + 2),
+                "the ring holds one f32 row and its norm weights in the row phase");
   auto kern = row_fused_kernel<IO, BN, SWAP, STAGES>;
   PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-  // Re-plan with the cluster sizes this kernel can co-schedule.
-  {
-    ClusterCaps caps;
-    query_cluster_caps(kern, kGemmThreads, L::kBytes, caps.max_active);
-    const GemmPlan p = plan_gemm(args.g.T, args.g.N, args.g.K, c->sm_count, kSplitScratchBytes, true, &caps,
-                                 true);
-    args.g.dp_rounds = p.dp_rounds;
-    args.g.sk_first = p.sk_first;
-    args.g.grid = p.grid;
-    args.g.sk_grid = p.sk_grid;
-    args.g.max_contrib = p.max_contrib;
-    args.g.csk = p.csk;
-    args.g.n_clusters = p.n_clusters;
-  }
+  if (args.g.nsplit > 1 && split_recv_bytes(BN, args.g.nsplit) > static_cast<size_t>(STAGES) * L::kStageBytes)
+    return set_error(PGB_ERR_STATE, "row kernel: split of %d does not fit the pipeline ring", args.g.nsplit);
   constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
   const int T = args.g.T, N = args.g.N, K = args.g.K;
   CUtensorMap tm_x, tm_w;
@@ -395,15 +309,14 @@ int launch_row(pgb_comm* c, RowArgs args, const void* x, const void* w, cudaStre
   if (rc) return rc;
 
   cudaLaunchConfig_t cfg{};
-  // Every SM takes part in the reduction phases; a cluster split-K launch
-  // has exactly n_clusters * csk CTAs.
-  cfg.gridDim = dim3(args.g.csk > 1 ? args.g.n_clusters * args.g.csk : c->sm_count);
+  // Every SM takes part in the row phase.
+  cfg.gridDim = dim3(c->sm_count);
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   const CUtensorMap& ta = SWAP ? tm_w : tm_x;
   const CUtensorMap& tb = SWAP ? tm_x : tm_w;
-  return launch_ex(cfg, /*cooperative=*/true, args.g.csk, kern, ta, tb, args);
+  return launch_ex(cfg, /*cooperative=*/true, 1, kern, ta, tb, args);
 }
 
 template <typename IO>
@@ -488,9 +401,9 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
     return set_error(PGB_ERR_INVALID,
                      "row_gemm: %d x %d payload exceeds the communicator buffer (max_bytes=%zu)", T,
                      N, comm->max_bytes);
-  const GemmPlan p = plan_gemm(T, N, K_local, comm->sm_count, kSplitScratchBytes, /*all_streamk=*/true);
+  const GemmPlan p = plan_gemm(T, N, K_local, comm->sm_count, kSplitScratchBytes);
   if (p.counter_bytes > kTileCounterBytes)
-    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: too many tiles (%d)", p.tiles);
+    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: too many split tiles (%d)", p.tiles - p.split_first);
 
   RowArgs args{};
   args.g.T = T;
@@ -501,15 +414,13 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
   args.g.q_tiles = p.q_tiles;
   args.g.tiles = p.tiles;
   args.g.dp_rounds = p.dp_rounds;
-  args.g.sk_first = p.sk_first;
+  args.g.split_first = p.split_first;
   args.g.grid = p.grid;
-  args.g.sk_grid = p.sk_grid;
-  args.g.max_contrib = p.max_contrib;
-  args.g.csk = p.csk;
-  args.g.n_clusters = p.n_clusters;
+  args.g.split_ctas = p.split_ctas;
+  args.g.nsplit = p.nsplit;
   args.g.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
-  args.g.ws = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
-  args.grid_bar = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kGridBar);
+  args.g.ctr = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kCounters);
+  args.g.xchg = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
   args.g.wait_ns = 2000000000ull;
   args.cm = comm_dev(comm);
   args.rs = rs;

@@ -112,6 +112,20 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Untiled bulk copy global -> shared, completion counted on `bar`
+// (complete_tx). Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses (and what its acquires
+// made visible) before its later async-proxy accesses to global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // L2 eviction-priority policies for cp.async.bulk cache hints (createpolicy).
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
@@ -256,6 +270,17 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   return v;
 }
 // Arrive (release at cluster scope) on an mbarrier of another CTA.
+// 16-byte store into a peer CTA's shared memory; the bytes are counted on
+// the peer's mbarrier (complete_tx), so the peer learns of their arrival by
+// waiting on it.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, uint32_t a, uint32_t b, uint32_t c,
+                                            uint32_t d, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+          remote_addr),
+      "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
+      : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
 }
@@ -329,8 +354,10 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as
 constexpr int kTraceSlots = 1024;
 __device__ uint64_t* pgb_trace_buf;
 __device__ __forceinline__ void trace(int slot) {
-  if (pgb_trace_buf != nullptr && slot < kTraceSlots)
-    pgb_trace_buf[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = globaltimer_ns();
+  // Read-only path for the pointer: a trace point must not add a memory
+  // round trip to the code it measures.
+  uint64_t* buf = reinterpret_cast<uint64_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&pgb_trace_buf)));
+  if (buf != nullptr && slot < kTraceSlots) buf[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = globaltimer_ns();
 }
 #else
 __device__ __forceinline__ void trace(int) {}
