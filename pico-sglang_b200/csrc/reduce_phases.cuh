@@ -37,11 +37,16 @@ static __device__ __noinline__ bool grid_cross_barrier(const CommDev& cm, int ba
     // peer memory) are ordered before its arrival, and the last CTA acquires
     // them all before it publishes the flag (system scope across GPUs).
     const uint32_t old = atom_add_acqrel_gpu(&cm.arrive[bar], 1u);
+    if (bar == 0) trace(1020);
     if (old == gridDim.x - 1) {
       cm.arrive[bar] = 0u;
       if (sys_scope) {
+        // One system-scope fence, then relaxed flag stores: each
+        // st.release.sys would repeat the fence.
         __threadfence_system();
-        for (int r = 0; r < cm.world; ++r) st_release_sys(&cm.flags[r][bar * PGB_MAX_RANKS + cm.rank], e);
+        if (bar == 0) trace(1021);
+        for (int r = 0; r < cm.world; ++r) st_relaxed_sys(&cm.flags[r][bar * PGB_MAX_RANKS + cm.rank], e);
+        if (bar == 0) trace(1022);
       } else {  // one GPU: its own flag, device scope
         st_release_gpu(&cm.flags[cm.rank][bar * PGB_MAX_RANKS + cm.rank], e);
       }
