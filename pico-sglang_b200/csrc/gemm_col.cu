@@ -4,6 +4,7 @@
 // LinearTPImpl.forward (python/picosgl/layers/linear.py:23-27) for the
 // column-parallel layers LinearColParallelMerged / LinearColParallelPartitioned
 // (linear.py:45-73). No collective follows a column-parallel GEMM.
+#include "gemm_f32.h"
 #include "gemm_plan.h"
 #include "gemm_sm100.cuh"
 #include "host_common.h"
@@ -234,8 +235,16 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
   if (T < 0 || N <= 0 || K <= 0)
     return set_error(PGB_ERR_INVALID, "col_gemm: bad shape T=%d N=%d K=%d", T, N, K);
   if (T == 0) return PGB_OK;
+  if (dtype == PGB_F32) {
+    // f32 check mode: CUDA-core GEMM, no workspace.
+    if (x == nullptr || w == nullptr || y == nullptr)
+      return set_error(PGB_ERR_INVALID, "col_gemm: null pointer argument");
+    return launch_gemm_f32(static_cast<const float*>(x), static_cast<const float*>(w),
+                           static_cast<const float*>(bias), static_cast<float*>(y), T, N, K,
+                           static_cast<cudaStream_t>(stream));
+  }
   if (dtype != PGB_BF16 && dtype != PGB_F16)
-    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: dtype %d not supported (bf16/f16 only)", dtype);
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: dtype %d not supported", dtype);
   if (K % 8 != 0 || N % 8 != 0)
     return set_error(PGB_ERR_INVALID, "col_gemm: K=%d and N=%d must be multiples of 8", K, N);
   if (x == nullptr || w == nullptr || y == nullptr || workspace == nullptr)

@@ -19,6 +19,7 @@
 //   Two-shot owners also push both rows to every peer's result region.
 // Barrier 1 + phase 3 (two-shot only): copy the other owners' rows in.
 #include "comm.h"
+#include "gemm_f32.h"
 #include "gemm_plan.h"
 #include "gemm_sm100.cuh"
 #include "host_common.h"
@@ -334,6 +335,30 @@ int dispatch_row(pgb_comm* c, const GemmPlan& p, const RowArgs& args, const void
 
 }  // namespace
 
+// f32 check mode of the fused row op: the partial product in IEEE f32 into
+// `out`, the communicator's all-reduce over it, then the f32 fused
+// residual-add + RMSNorm - the reference's sequence (linear.py:90-97,
+// pynccl.cu:95-137, norm.py:73-75) at f32, as separate launches (not a hot
+// path). The bias, if any, is added on every rank before the reduction, as
+// in the fused bf16 kernel.
+int row_f32(pgb_comm* comm, const void* x_local, const void* w_local, const void* bias, void* residual,
+            const void* norm_w, float eps, void* out, int T, int N, int K_local, void* stream) {
+  if (x_local == nullptr || w_local == nullptr || out == nullptr)
+    return set_error(PGB_ERR_INVALID, "row_gemm: null pointer argument");
+  if (norm_w != nullptr && residual == nullptr)
+    return set_error(PGB_ERR_INVALID, "row_gemm: norm weight given without residual");
+  int rc = launch_gemm_f32(static_cast<const float*>(x_local), static_cast<const float*>(w_local),
+                           static_cast<const float*>(bias), static_cast<float*>(out), T, N, K_local,
+                           static_cast<cudaStream_t>(stream));
+  if (rc) return rc;
+  if (comm->world > 1) {
+    rc = pgb_all_reduce(comm, out, static_cast<size_t>(T) * N, PGB_F32, PGB_OP_SUM, stream);
+    if (rc) return rc;
+  }
+  if (norm_w != nullptr) rc = pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, PGB_F32, stream);
+  return rc;
+}
+
 // Choose one-shot or two-shot for a reduction of `rows` x `width` elements of
 // `elem` bytes; returns false if neither fits the communicator buffers.
 bool plan_rows(const pgb_comm* c, int rows, int width, int elem, RowSplit* rs) {
@@ -373,8 +398,7 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
   if (T < 0 || N <= 0 || K_local <= 0)
     return set_error(PGB_ERR_INVALID, "row_gemm: bad shape T=%d N=%d K=%d", T, N, K_local);
   if (T == 0) return PGB_OK;
-  if (dtype == PGB_F32)
-    return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: f32 is served by the check-mode path");
+  if (dtype == PGB_F32) return row_f32(comm, x_local, w_local, bias, residual, norm_w, eps, out, T, N, K_local, stream);
   if (dtype != PGB_BF16 && dtype != PGB_F16)
     return set_error(PGB_ERR_INVALID, "row_gemm: unknown dtype %d", dtype);
   if (K_local % 8 != 0 || N % 8 != 0)

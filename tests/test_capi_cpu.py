@@ -55,7 +55,7 @@ def test_gemm_rejects_bad_arguments_before_touching_the_device(pgb):
     lib = pgb._lib.load()
     rc = lib.pgb_col_gemm(1, 1, None, 1, 4, 16, 12, pgb._lib.PGB_BF16, 1, 1 << 20, None)
     assert rc == pgb._lib.PGB_ERR_INVALID and "multiples of 8" in _last_error(lib)
-    rc = lib.pgb_col_gemm(1, 1, None, 1, 4, 16, 16, pgb._lib.PGB_F32, 1, 1 << 20, None)
+    rc = lib.pgb_col_gemm(1, 1, None, 1, 4, 16, 16, 7, 1, 1 << 20, None)  # no such dtype
     assert rc == pgb._lib.PGB_ERR_UNSUPPORTED
     rc = lib.pgb_col_gemm(1, 1, None, 1, -1, 16, 16, pgb._lib.PGB_BF16, 1, 1 << 20, None)
     assert rc == pgb._lib.PGB_ERR_INVALID

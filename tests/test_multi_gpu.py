@@ -139,6 +139,24 @@ def _worker(rank: int, world: int, port: int, case: str, q):
                 dist.all_gather_object(objs, (o.float().sum().item(), rr.float().sum().item()))
                 out[f"same_{T}_{H}_{K}"] = (len(set(objs)) == 1, str(objs))
                 del gathered
+            # f32 check mode: IEEE f32 GEMM + all-reduce + add/RMSNorm, 1e-5 relative
+            T, H, K = 8, 4096, 4096
+            g = torch.Generator(device=dev).manual_seed(17)
+            xf = torch.randn(T, K, device=dev, generator=g)
+            wf = torch.randn(H, K, device=dev, generator=g) * 0.02
+            rf = torch.randn(T, H, device=dev, generator=g)
+            nwf = torch.rand(H, device=dev, generator=g) + 0.5
+            k0, k1 = rank * K // world, (rank + 1) * K // world
+            rr32 = rf.clone()
+            o32 = pgb.ops.row_gemm_allreduce_addnorm(comm, xf[:, k0:k1].contiguous(), wf[:, k0:k1].contiguous(),
+                                                     rr32, nwf, EPS)
+            torch.cuda.synchronize()
+            s64 = xf.double() @ wf.double().t() + rf.double()
+            ref64 = s64 * torch.rsqrt(s64.pow(2).mean(-1, keepdim=True) + EPS) * nwf.double()
+            rms = ref64.pow(2).mean().sqrt().item()
+            e_out = (o32.double() - ref64).abs().max().item() / rms
+            e_res = (rr32.double() - s64).abs().max().item() / s64.pow(2).mean().sqrt().item()
+            out["f32_check"] = (e_out <= 1e-5 and e_res <= 1e-5, f"rel err out {e_out:.3g} residual {e_res:.3g}")
             # graph replay
             T, H, K = 16, 4096, 4096
             g = torch.Generator(device=dev).manual_seed(5)
