@@ -27,7 +27,7 @@ __device__ __forceinline__ uint32_t comm_begin(const CommDev& cm) {
 // early when another CTA already recorded an error. Every CTA must call this
 // with the same `bar` sequence, errors or not, so counters stay balanced.
 // sys_scope = false (one GPU) only synchronises the grid, at device scope.
-static __device__ __noinline__ bool grid_cross_barrier(const CommDev& cm, int bar, uint32_t e,
+__device__ __forceinline__ bool grid_cross_barrier(const CommDev& cm, int bar, uint32_t e,
                                                    bool sys_scope) {
   __shared__ int s_ok;
   __syncthreads();
@@ -232,7 +232,7 @@ __device__ __forceinline__ void unpack8_io(const uint4& u, float* v) {
 // in shared memory `srow` (width f32 + width IO values) for the second pass,
 // which only reads shared memory and stores. IO is 16-bit.
 template <typename IO, int MAXV>
-__device__ __noinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity, int t, int width,
+__device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity, int t, int width,
                                         IO* out, IO* residual, const IO* norm_w, float eps, int do_norm, float* red,
                                         float* srow) {
   static_assert(sizeof(IO) == 2, "16-bit I/O");
@@ -307,6 +307,119 @@ __device__ __noinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, u
   }
   // srow is reused by the next row of this CTA.
   __syncthreads();
+}
+
+// Phase 2 with one warp per row, for launches with more rows than CTAs
+// (prefill, and wide decode batches): every warp of the grid reduces its own
+// rows, so rows proceed in parallel instead of one after another per CTA.
+// Same arithmetic as reduce_row. Each lane requests the source and residual
+// vectors of 8 vectors at a time; the warp's f32 pre-norm row waits in its
+// slice of `stage` (width * 4 bytes per warp), the norm weights are staged
+// once per CTA after those slices; the sum of squares is reduced with
+// shuffles. Called by every thread of the CTA. IO is 16-bit.
+template <typename IO>
+__device__ __forceinline__ void reduce_rows_warp(const CommDev& cm, const RowSplit& rs, uint32_t parity, int r0,
+                                                 int r1, int width, IO* out, IO* residual, const IO* norm_w,
+                                                 float eps, int do_norm, uint8_t* stage) {
+  static_assert(sizeof(IO) == 2, "16-bit I/O");
+  constexpr int kBatch = 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int nvec = width >> 3;
+  float* srow = reinterpret_cast<float*>(stage) + static_cast<size_t>(warp) * width;
+  uint4* wrow = reinterpret_cast<uint4*>(reinterpret_cast<float*>(stage) + static_cast<size_t>(nwarps) * width);
+  if (do_norm) {
+#pragma unroll 1
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) wrow[v] = __ldg(reinterpret_cast<const uint4*>(norm_w) + v);
+  }
+  __syncthreads();
+  const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
+  const bool push = !rs.oneshot && cm.world > 1;
+#pragma unroll 1
+  for (int t = r0 + static_cast<int>(blockIdx.x) * nwarps + warp; t < r1; t += gridDim.x * nwarps) {
+    const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
+    const IO* slot0 = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes) +
+                      static_cast<size_t>(lr) * width;
+    const size_t row_off = static_cast<size_t>(t) * width;
+    float ss = 0.f;
+#pragma unroll 1
+    for (int v0 = lane; v0 < nvec; v0 += 32 * kBatch) {
+      uint4 sv[kBatch], rr[kBatch];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int v = min(v0 + 32 * b, nvec - 1);  // clamped: lanes past the row re-read its last vector
+        sv[b] = __ldcg(reinterpret_cast<const uint4*>(slot0) + v);
+        // residual is null without the norm.
+        rr[b] = do_norm ? __ldcg(reinterpret_cast<const uint4*>(residual + row_off) + v) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      float acc[kBatch][8];
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) unpack8_io<IO>(sv[b], acc[b]);
+#pragma unroll 1
+      for (int d = 1; d < cm.world; ++d) {
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b)
+          sv[b] = __ldcg(reinterpret_cast<const uint4*>(slot0 + d * src_stride) + min(v0 + 32 * b, nvec - 1));
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          float p[8];
+          unpack8_io<IO>(sv[b], p);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[b][j] += p[j];
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kBatch; ++b) {
+        const int v = v0 + 32 * b;
+        const bool in = v < nvec;
+        float p[8];
+        unpack8_io<IO>(rr[b], p);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          acc[b][j] = round_io<IO>(acc[b][j]);
+          if (do_norm) acc[b][j] += p[j];
+          if (do_norm && in) ss += acc[b][j] * acc[b][j];
+        }
+        if (in) {
+          float4* dst = reinterpret_cast<float4*>(srow) + 2 * v;
+          dst[0] = make_float4(acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
+          dst[1] = make_float4(acc[b][4], acc[b][5], acc[b][6], acc[b][7]);
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rcp = do_norm ? rsqrtf(ss / static_cast<float>(width) + eps) : 1.f;
+    __syncwarp();
+#pragma unroll 1
+    for (int v = lane; v < nvec; v += 32) {
+      const float4 a = reinterpret_cast<const float4*>(srow)[2 * v];
+      const float4 b = reinterpret_cast<const float4*>(srow)[2 * v + 1];
+      float s8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      float o[8];
+      if (do_norm) {
+        float w[8];
+        unpack8_io<IO>(wrow[v], w);
+        store8<IO>(residual + row_off + v * 8, s8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = s8[j] * rcp * w[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = s8[j];
+      }
+      store8<IO>(out + row_off + v * 8, o);
+      if (push) {
+#pragma unroll 1
+        for (int d = 0; d < cm.world; ++d) {
+          if (d == cm.rank) continue;
+          uint8_t* base = cm.results[d] + parity * cm.result_parity_bytes;
+          store8<IO>(reinterpret_cast<IO*>(base) + row_off + v * 8, o);
+          if (do_norm) store8<IO>(reinterpret_cast<IO*>(base + cm.result_parity_bytes / 2) + row_off + v * 8, s8);
+        }
+      }
+    }
+    __syncwarp();  // srow is reused by this warp's next row
+  }
 }
 
 // Phase 3 (two-shot): copy the rows owned by other ranks from this rank's

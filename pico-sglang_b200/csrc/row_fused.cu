@@ -268,13 +268,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) trace(1002);
   if (ok0) {
     const int r0 = a.rs.first(a.cm.rank), r1 = a.rs.last(a.cm.rank);
-    // The pipeline ring is idle from here on: it holds the f32 pre-norm row.
-    float* srow = reinterpret_cast<float*>(c.a);
-    int nrow = 0;
-    for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x, ++nrow) {
-      reduce_row<IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps, a.do_norm, s_red,
-                                 srow);
-      if (threadIdx.x == 0 && nrow < 3) trace(1017 + nrow);
+    // The pipeline ring is idle from here on: it stages the pre-norm rows.
+    constexpr size_t kRing = static_cast<size_t>(STAGES) * GemmSmem<BN, STAGES>::kStageBytes;
+    if (r1 - r0 > static_cast<int>(gridDim.x) &&
+        static_cast<size_t>(g.N) * (4u * (kGemmThreads / 32) + 2u) <= kRing) {
+      reduce_rows_warp<IO>(a.cm, a.rs, parity, r0, r1, g.N, out, residual, norm_w, a.eps, a.do_norm, c.a);
+      if (threadIdx.x == 0) trace(1017);
+    } else {
+      float* srow = reinterpret_cast<float*>(c.a);
+      int nrow = 0;
+      for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x, ++nrow) {
+        reduce_row<IO, kRowMaxVec>(a.cm, a.rs, parity, t, g.N, out, residual, norm_w, a.eps, a.do_norm, s_red,
+                                   srow);
+        if (threadIdx.x == 0 && nrow < 3) trace(1017 + nrow);
+      }
     }
   }
   if (multi && !a.rs.oneshot) {
