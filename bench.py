@@ -50,6 +50,7 @@ EPS = 1e-6
 TOKENS = (1, 8, 32, 128, 256)
 HEADLINE_T = 256
 L2_BYTES = 126 * 2**20
+GATE_UP_T256_TP1_DRAM_BYTES = 207_560_960  # 203.54 MB read + 4.02 MB written (ncu, one launch)
 
 
 def load_peaks() -> dict:
@@ -421,7 +422,9 @@ def run_ours(args) -> dict | None:
                 "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "peak_src": peaks["src"] + " (burst copy bandwidth)",
-                "traffic": None,
+                # DRAM read + write bytes of one gate_up launch at T=256, TP=1, from the
+                # ncu capture summarised in profiles/col_gemm_gate_up_T256.md.
+                "traffic": GATE_UP_T256_TP1_DRAM_BYTES if (n == 1 and T == 256) else None,
                 "algorithmic_bytes_per_launch": gu_bytes,
                 "avg_launch_us": round(gu_us, 3),
             },
