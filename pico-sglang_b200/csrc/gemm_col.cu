@@ -12,7 +12,7 @@
 namespace pgb {
 
 template <typename IO, int BN, bool SWAP, int STAGES>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
     col_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     GemmShape g, IO* __restrict__ y, const IO* __restrict__ bias) {
   extern __shared__ uint8_t smem_raw[];

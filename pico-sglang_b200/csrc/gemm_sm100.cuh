@@ -152,12 +152,19 @@ struct GemmSmem {
   static constexpr int kBytes = kOffBar + kBarBytes + 1024;  // + alignment slack
 };
 
-// Pipeline depth that fills the shared-memory budget for a tile width.
+// CTAs per SM a GEMM kernel of tile width BN is built for. Narrow decode
+// tiles (BN <= 64) fit two CTAs per SM, so the next kernel in the stream
+// (programmatic dependent launch) becomes resident next to this one, sets up
+// and requests its first weight stages while this kernel finishes its tail.
+__host__ __device__ constexpr int gemm_ctas_per_sm(int bn) { return bn <= 64 ? 2 : 1; }
+
+// Pipeline depth that fills the shared-memory budget for a tile width:
+// ~100 KB of ring when two CTAs share an SM, ~200 KB otherwise (room is left
+// for the epilogue tile and the barriers).
 __host__ __device__ constexpr int gemm_stages_for(int bn) {
-  // 200 KB leaves room for the epilogue tile and the barriers.
-  return (200 * 1024) / (kTileP * kBlockK * 2 + bn * kBlockK * 2) > 12
+  return ((gemm_ctas_per_sm(bn) == 2 ? 100 : 200) * 1024) / (kTileP * kBlockK * 2 + bn * kBlockK * 2) > 12
              ? 12
-             : (200 * 1024) / (kTileP * kBlockK * 2 + bn * kBlockK * 2);
+             : ((gemm_ctas_per_sm(bn) == 2 ? 100 : 200) * 1024) / (kTileP * kBlockK * 2 + bn * kBlockK * 2);
 }
 template <int BN>
 constexpr int gemm_stages() {
@@ -296,6 +303,9 @@ __device__ __forceinline__ void gemm_producer(const GemmShape& g, const GemmCtl&
 template <int BN, int STAGES>
 __device__ __forceinline__ void gemm_mma(const GemmShape& g, const GemmCtl& c, uint32_t idesc) {
   using L = GemmSmem<BN, STAGES>;
+  // The first activation tiles arrive only after the predecessor kernel has
+  // finished; start the bounded waits from there.
+  pdl_wait();
   int stage = 0;
   uint32_t phase = 0;
   int acc = 0;

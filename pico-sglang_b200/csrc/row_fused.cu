@@ -119,7 +119,7 @@ __device__ __forceinline__ void row_store_partial_vec32(const RowArgs& a, uint32
 }
 
 template <typename IO, int BN, bool SWAP, int STAGES>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
     row_fused_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                      RowArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -270,11 +270,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int r0 = a.rs.first(a.cm.rank), r1 = a.rs.last(a.cm.rank);
     // The pipeline ring is idle from here on: it stages the pre-norm rows.
     constexpr size_t kRing = static_cast<size_t>(STAGES) * GemmSmem<BN, STAGES>::kStageBytes;
-    if (r1 - r0 > static_cast<int>(gridDim.x) &&
-        static_cast<size_t>(g.N) * (4u * (kGemmThreads / 32) + 2u) <= kRing) {
-      reduce_rows_warp<IO>(a.cm, a.rs, parity, r0, r1, g.N, out, residual, norm_w, a.eps, a.do_norm, c.a);
-      if (threadIdx.x == 0) trace(1017);
-    } else {
+    // Narrow (decode) tiles never carry more rows than CTAs: only wide tiles
+    // build the warp-per-row path.
+    bool warp_rows = false;
+    if constexpr (BN >= 128) {
+      if (r1 - r0 > static_cast<int>(gridDim.x) &&
+          static_cast<size_t>(g.N) * (4u * (kGemmThreads / 32) + 2u) <= kRing) {
+        reduce_rows_warp<IO>(a.cm, a.rs, parity, r0, r1, g.N, out, residual, norm_w, a.eps, a.do_norm, c.a);
+        if (threadIdx.x == 0) trace(1017);
+        warp_rows = true;
+      }
+    }
+    if (!warp_rows) {
       float* srow = reinterpret_cast<float*>(c.a);
       int nrow = 0;
       for (int t = r0 + static_cast<int>(blockIdx.x); t < r1; t += gridDim.x, ++nrow) {
