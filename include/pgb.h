@@ -181,19 +181,20 @@ PGB_API int pgb_rmsnorm(const void* x, const void* w, float eps, void* out, int 
 
 /* ----------------------------------------------------------- diagnostics --
  * Replay on the host the work decomposition a GEMM of this shape would use
- * on `sms` SMs (all_streamk != 0: the row-parallel kernel's plan) with
- * launch_grid CTAs (0: the planned grid), with cluster split-K candidates
- * when clusters != 0 (B200 cluster capacities scaled to sms), and check that
- * it covers every tile and k-block exactly once with consistent contributor
- * bookkeeping. Needs no GPU. Internal consistency check, no reference
- * counterpart. */
+ * on `sms` SMs (all_streamk != 0: the row-parallel kernel's plan, whose
+ * split-tile exchange area is the communicator's) with launch_grid CTAs (0:
+ * the planned grid), and check that it covers every tile and k-block exactly
+ * once, gives every split tile its CTAs with distinct k-ranges, cuts the
+ * split tiles' tokens into contiguous runs, and fits the exchange area and
+ * the pipeline ring. `clusters` is ignored (kept for ABI stability). Needs no
+ * GPU. Internal consistency check, no reference counterpart. */
 PGB_API int pgb_check_work_plan(int T, int N, int K, int sms, int all_streamk, int launch_grid,
                                 int clusters);
 
 /* Write a one-line description of the work decomposition plan_gemm picks
  * for this shape (fused_row != 0: the fused row-parallel kernel) into
- * out[out_bytes], using B200 cluster capacities scaled to sms when
- * clusters != 0. Diagnostic, no reference counterpart. */
+ * out[out_bytes]. `clusters` is ignored (kept for ABI stability).
+ * Diagnostic, no reference counterpart. */
 PGB_API int pgb_describe_plan(int T, int N, int K, int sms, int fused_row, int clusters, char* out,
                               size_t out_bytes);
 

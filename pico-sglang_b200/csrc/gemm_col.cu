@@ -272,8 +272,8 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
 // GEMM. Examples are a serving runtime that has already handed nearly all of
 // HBM to its KV-cache pool, an allocator hook that must not re-enter the
 // allocator, and code on a latency path where cudaMalloc/cudaFree would
-// synchronise the device. pgb_col_gemm_noalloc serves them: its stream-K
-// scratch is a fixed array inside this library's device image, so the call
+// synchronise the device. pgb_col_gemm_noalloc serves them: its split-K
+// scratch (status word, split-tile counters, exchange area) is a fixed array inside this library's device image, so the call
 // itself allocates nothing.
 //
 // Limits and rules:

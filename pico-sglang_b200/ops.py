@@ -37,7 +37,7 @@ def _stream(t: torch.Tensor) -> int:
 
 
 class _Workspaces:
-    """Per-device zero-initialised scratch for split-K partials and tile counters.
+    """Per-device zero-initialised scratch: split-tile counters and the split-K exchange area.
 
     Grows outside CUDA-graph capture; inside a capture the size must already be
     sufficient (allocation during capture would not be replayed)."""
