@@ -252,12 +252,20 @@ __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs
       wv = __ldg(reinterpret_cast<const uint4*>(norm_w) + v);
     }
     float s8[8], p[8];
-    unpack8_io<IO>(__ldcg(reinterpret_cast<const uint4*>(slot0) + v), s8);
-#pragma unroll 1
-    for (int d = 1; d < cm.world; ++d) {
-      unpack8_io<IO>(__ldcg(reinterpret_cast<const uint4*>(slot0 + d * src_stride) + v), p);
+    // Every rank's slot requested before the first add (one round trip, not
+    // one per rank); the sum stays in rank order.
+    uint4 sv[PGB_MAX_RANKS];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s8[j] += p[j];
+    for (int d = 0; d < PGB_MAX_RANKS; ++d)
+      if (d < cm.world) sv[d] = __ldcg(reinterpret_cast<const uint4*>(slot0 + d * src_stride) + v);
+    unpack8_io<IO>(sv[0], s8);
+#pragma unroll
+    for (int d = 1; d < PGB_MAX_RANKS; ++d) {
+      if (d < cm.world) {
+        unpack8_io<IO>(sv[d], p);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s8[j] += p[j];
+      }
     }
 #pragma unroll
     for (int j = 0; j < 8; ++j) s8[j] = round_io<IO>(s8[j]);
@@ -428,23 +436,40 @@ template <typename IO>
 __device__ __forceinline__ void gather_rows(const CommDev& cm, const RowSplit& rs, uint32_t parity,
                                             int width, IO* out, IO* residual, int do_norm) {
   const uint8_t* base = cm.results[cm.rank] + parity * cm.result_parity_bytes;
-  const IO* out_plane = reinterpret_cast<const IO*>(base);
-  const IO* res_plane = reinterpret_cast<const IO*>(base + cm.result_parity_bytes / 2);
-  const int r0 = rs.first(cm.rank), r1 = rs.last(cm.rank);
-  const int nvec = width >> 3;
-  const long long total = static_cast<long long>(rs.rows) * nvec;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int t = static_cast<int>(i / nvec);
-    if (t >= r0 && t < r1) continue;
-    const size_t off = static_cast<size_t>(t) * width + (i % nvec) * 8;
-    constexpr int kU4 = static_cast<int>(sizeof(IO)) / 2;  // 16-byte words per 8 elements
+  const uint4* out_plane = reinterpret_cast<const uint4*>(base);
+  const uint4* res_plane = reinterpret_cast<const uint4*>(base + cm.result_parity_bytes / 2);
+  // The rows owned by other ranks are two contiguous ranges, [0, r0) and
+  // [r1, rows): copy them as 16-byte words, 4 per thread and step with the
+  // loads issued before the stores.
+  const size_t row_words = static_cast<size_t>(width) * sizeof(IO) / 16;
+  const size_t r0 = static_cast<size_t>(rs.first(cm.rank)), r1 = static_cast<size_t>(rs.last(cm.rank));
+  const size_t nthr = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t me = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  uint4* o4 = reinterpret_cast<uint4*>(out);
+  uint4* r4 = reinterpret_cast<uint4*>(residual);
+#pragma unroll 1
+  for (int part = 0; part < 2; ++part) {
+    const size_t w0 = part == 0 ? 0 : r1 * row_words;
+    const size_t w1 = part == 0 ? r0 * row_words : static_cast<size_t>(rs.rows) * row_words;
+#pragma unroll 1
+    for (size_t i = w0 + me; i < w1; i += 4 * nthr) {
+      uint4 ov[4], rv[4];
 #pragma unroll
-    for (int k = 0; k < kU4; ++k) {
-      reinterpret_cast<uint4*>(out + off)[k] = __ldcg(reinterpret_cast<const uint4*>(out_plane + off) + k);
-      if (do_norm)
-        reinterpret_cast<uint4*>(residual + off)[k] =
-            __ldcg(reinterpret_cast<const uint4*>(res_plane + off) + k);
+      for (int k = 0; k < 4; ++k) {
+        const size_t j = i + k * nthr;
+        if (j < w1) {
+          ov[k] = __ldcg(out_plane + j);
+          if (do_norm) rv[k] = __ldcg(res_plane + j);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const size_t j = i + k * nthr;
+        if (j < w1) {
+          o4[j] = ov[k];
+          if (do_norm) r4[j] = rv[k];
+        }
+      }
     }
   }
 }

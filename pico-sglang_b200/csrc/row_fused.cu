@@ -292,7 +292,9 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
     }
   }
   if (multi && !a.rs.oneshot) {
+    if (threadIdx.x == 0) trace(1008);
     const bool ok2 = grid_cross_barrier(a.cm, kBarResults, e, true);
+    if (threadIdx.x == 0) trace(1009);
     if (ok0 && ok2) gather_rows<IO>(a.cm, a.rs, parity, g.N, out, residual, a.do_norm);
   }
   if (threadIdx.x == 0) trace(1003);
