@@ -41,9 +41,11 @@ __device__ __forceinline__ bool grid_cross_barrier(const CommDev& cm, int bar, u
     if (old == gridDim.x - 1) {
       cm.arrive[bar] = 0u;
       if (sys_scope) {
-        // One system-scope fence, then relaxed flag stores: each
-        // st.release.sys would repeat the fence.
-        __threadfence_system();
+        // One acquire-release fence at system scope, then relaxed flag
+        // stores (a release pattern for each of them): each st.release.sys
+        // would repeat the fence, and a sequentially consistent fence is
+        // not needed.
+        fence_acq_rel_sys();
         if (bar == 0) trace(1021);
         for (int r = 0; r < cm.world; ++r) st_relaxed_sys(&cm.flags[r][bar * PGB_MAX_RANKS + cm.rank], e);
         if (bar == 0) trace(1022);
@@ -344,7 +346,10 @@ __device__ __forceinline__ void reduce_rows_warp(const CommDev& cm, const RowSpl
   const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
   const bool push = !rs.oneshot && cm.world > 1;
 #pragma unroll 1
-  for (int t = r0 + static_cast<int>(blockIdx.x) * nwarps + warp; t < r1; t += gridDim.x * nwarps) {
+  // Rows go to CTAs first, then to warps: the rows spread over every SM
+  // instead of filling a few SMs six warps deep.
+  for (int t = r0 + warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x); t < r1;
+       t += gridDim.x * nwarps) {
     const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
     const IO* slot0 = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes) +
                       static_cast<size_t>(lr) * width;
