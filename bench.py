@@ -13,8 +13,10 @@ LlamaDecoderLayer.forward (models/llama.py:77-86), built from this repo's
 public layer classes: qkv_proj (column GEMM) -> o_proj fused with the
 all-reduce and post_attention_layernorm -> gate_up_proj (column GEMM) on that
 norm's output -> down_proj fused with the all-reduce and the next layer's
-input_layernorm. Attention and silu_and_mul are outside the path; their
-outputs are fixed synthetic activations. L is chosen so the step's weights
+input_layernorm. Attention and silu_and_mul are outside the step; their
+outputs are fixed synthetic activations. The gated MLP's front half
+(gate_up_proj + silu_and_mul, fused by pgb_gate_up_silu) is timed beside the
+step under `config.mlp_front_us`. L is chosen so the step's weights
 exceed 3x the 126 MB L2, so every layer streams its weights from HBM (no L2
 flush is needed). The step is captured once in a CUDA graph (as the
 reference's decode graphs, engine/graph.py:100-142) and replayed.
@@ -342,6 +344,7 @@ def run_ours(args) -> dict | None:
         breakdown[name] = round(ms_op * 1000.0 / args.steps / n_layers, 3)
         del gg
     breakdown["gate_up"] = round(gu_us, 3)
+    mlp_front = mlp_front_timings(args, pgb, layers, x1, stream, barrier, n_layers)
 
     # End to end through the public API: pinned host inputs copied in, the
     # captured layer stack replayed, the output and residual copied out.
@@ -410,6 +413,7 @@ def run_ours(args) -> dict | None:
                 "graph": "step captured in one CUDA graph and replayed",
                 "per_tokens": {str(k): v for k, v in per_t.items()},
                 "op_breakdown_us": breakdown,
+                "mlp_front_us": mlp_front,
                 "layer_roofline_us": head["roofline_us"],
                 "layer_frac_of_roofline": head["frac_of_roofline"],
             },
@@ -443,6 +447,47 @@ def run_ours(args) -> dict | None:
         D.destroy_distributed()
         dist.destroy_process_group()
     return result
+
+
+def mlp_front_timings(args, pgb, layers, x1, stream, barrier, n_layers) -> dict:
+    """The gated MLP's front half, gate_up_proj then silu_and_mul
+    (python/picosgl/layers/mlp.py:43-46), per layer at the headline T, three ways:
+    the fused kernel, this library's GEMM then its standalone activation, and
+    the reference's own calls (F.linear + flashinfer.silu_and_mul). Each is
+    captured over the L distinct layers and replayed like the step."""
+    import torch.nn.functional as F
+
+    ways = {
+        "fused_gate_up_silu": lambda lay: pgb.gate_up_silu(x1, lay["gate_up"].weight),
+        "col_gemm_then_silu_and_mul": lambda lay: pgb.silu_and_mul(pgb.col_gemm(x1, lay["gate_up"].weight)),
+    }
+    if args.library_baseline:
+        try:
+            import flashinfer
+
+            ways["F.linear_then_flashinfer_silu_and_mul"] = (
+                lambda lay: flashinfer.silu_and_mul(F.linear(x1, lay["gate_up"].weight)))
+        except Exception:  # pragma: no cover - flashinfer missing
+            pass
+    out = {"tokens": int(x1.shape[0])}
+    for name, fn in ways.items():
+        def f(fn=fn):
+            for lay in layers:
+                fn(lay)
+
+        with torch.cuda.stream(stream):
+            gg = capture(f, stream)
+            ms = time_graph(gg, stream, args.steps, args.warmup, barrier)
+        ms_t = torch.tensor([ms])
+        if dist_is_initialized():
+            torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+        out[name] = round(ms_t.item() * 1000.0 / args.steps / n_layers, 3)
+        del gg
+    return out
+
+
+def dist_is_initialized() -> bool:
+    return torch.distributed.is_available() and torch.distributed.is_initialized()
 
 
 def library_path_baseline(args, n, rank, world, dev, stream, barrier, T) -> dict:

@@ -123,7 +123,9 @@ PGB_API int pgb_all_gather(pgb_comm* comm, void* out, const void* in, size_t cou
  * x, w, y row-major, element type dtype (PGB_BF16 or PGB_F16), f32
  * accumulation, K % 8 == 0, N % 8 == 0. workspace is split-K scratch of at
  * least pgb_col_gemm_workspace_size(T, N, K) bytes, zero-filled once when it
- * is allocated (the kernels leave it zeroed again). Replaces
+ * is allocated: its status word and split-tile counters sit in a fixed head
+ * region that the kernels leave zeroed again, so calls of any shape may share
+ * one workspace when they are ordered on one stream. Replaces
  * LinearTPImpl.forward = F.linear (python/picosgl/layers/linear.py:23-27) for
  * LinearColParallelMerged / LinearColParallelPartitioned (linear.py:45-73). */
 PGB_API size_t pgb_col_gemm_workspace_size(int T, int N, int K);
@@ -147,6 +149,29 @@ PGB_API int pgb_col_gemm(const void* x, const void* w, const void* bias, void* y
  * Arguments and results are those of pgb_col_gemm. */
 PGB_API int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bias, void* y, int T, int N,
                                  int K, int dtype, void* stream);
+
+/* gate_up_proj GEMM with silu_and_mul in its epilogue:
+ *   gate_up  = x[T, K] . w[2I, K]^T (+ bias[2I]), rounded to dtype
+ *   out[T, I] = silu(gate_up[:, :I]) * gate_up[:, I:]   (f32, rounded once)
+ * w is the merged [gate; up] weight of LinearColParallelMerged
+ * (python/picosgl/layers/linear.py:45-56) as the loader fills it. Replaces
+ * GatedMLP.forward's gate_up_proj.forward + act_fn
+ * (python/picosgl/layers/mlp.py:43-46) -> silu_and_mul
+ * (python/picosgl/layers/activation.py:9-12); the [T, 2I] intermediate is
+ * never stored. bf16 / f16: K % 8 == 0, I % 8 == 0, out 16-byte aligned.
+ * f32 (check mode): the f32 GEMM into the workspace's exchange area, then
+ * pgb_silu_and_mul. workspace: at least
+ * pgb_gate_up_silu_workspace_size(T, I, K, dtype) bytes, zero-filled once
+ * when allocated; it may be the one pgb_col_gemm uses on the same stream. */
+PGB_API size_t pgb_gate_up_silu_workspace_size(int T, int I, int K, int dtype);
+PGB_API int pgb_gate_up_silu(const void* x, const void* w, const void* bias, void* out, int T, int I,
+                             int K, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[T, I] = silu(x[:, :I]) * x[:, I:] for x [T, 2I] row-major, SiLU and
+ * product in f32, rounded once to dtype (PGB_BF16, PGB_F16 or PGB_F32).
+ * Replaces silu_and_mul (python/picosgl/layers/activation.py:9-12) on a
+ * materialised gate_up tensor. */
+PGB_API int pgb_silu_and_mul(const void* x, void* out, int T, int I, int dtype, void* stream);
 
 /* Row-parallel GEMM fused with the all-reduce and the residual-add + RMSNorm
  * that consumes it:

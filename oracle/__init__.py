@@ -2,8 +2,9 @@
 
 This package restates, in numpy, what the reference (dakingffo/pico-sglang)
 computes on the path the CUDA library replaces: the column-parallel and
-row-parallel linears, the sum all-reduce that follows a row-parallel linear,
-and the residual-add + RMSNorm that consumes it.
+row-parallel linears, the gated MLP's silu_and_mul on the gate_up output,
+the sum all-reduce that follows a row-parallel linear, and the residual-add
++ RMSNorm that consumes it.
 
 It is the checker, never the product. Only tests/, __graft_entry__.smoke()
 and bench.py's CPU-baseline leg (and its --impl reference arm) may import
@@ -19,7 +20,10 @@ of FlashInfer's FusedAddRMSNormKernel (flashinfer/data/include/flashinfer/
 norm.cuh:387-470, a third-party dependency the reference calls at
 python/picosgl/layers/norm.py:74); no reference test exercises it, so on the
 CPU it is pinned to that published kernel only, and the GPU tests pin it to
-the installed flashinfer.fused_add_rmsnorm itself.
+the installed flashinfer.fused_add_rmsnorm itself. silu_and_mul restates
+flashinfer's act_and_mul kernel the same way; it is pinned on the CPU to the
+reference's GatedMLP run with that restatement as its act_fn (mlp_small.npz)
+and to torch.nn.functional.silu, and on the GPU to flashinfer.silu_and_mul.
 """
 
 from .tp_linear import (  # noqa: F401
@@ -27,10 +31,12 @@ from .tp_linear import (  # noqa: F401
     col_shard_merged,
     col_shard_partitioned,
     fused_add_rmsnorm,
+    gate_up_silu,
     linear,
     rmsnorm,
     round_to,
     row_parallel_addnorm,
     row_shard,
+    silu_and_mul,
     tp_layer_step,
 )

@@ -59,6 +59,30 @@ def linear(x, w, bias=None, dtype: str = "bf16", accum: str = "f64") -> np.ndarr
     return round_to(y, dtype)
 
 
+def silu_and_mul(gate_up, dtype: str = "bf16") -> np.ndarray:
+    """out = silu(g) * u for the halves g, u of gate_up's last dimension.
+
+    silu_and_mul (python/picosgl/layers/activation.py:9-12) calls
+    flashinfer.silu_and_mul (flashinfer 0.6.11, a third-party dependency not
+    vendored in the reference), whose act_and_mul kernel reads both halves,
+    computes g / (1 + exp(-g)) * u in float32 per element and casts the
+    result to the tensor's dtype once. Same steps here in float32 numpy.
+    """
+    a = np.asarray(gate_up, np.float32)
+    i = a.shape[-1] // 2
+    g, u = a[..., :i], a[..., i:]
+    with np.errstate(over="ignore"):
+        s = g / (np.float32(1.0) + np.exp(-g))
+    return round_to(s * u, dtype)
+
+
+def gate_up_silu(x, w_gate_up, bias=None, dtype: str = "bf16", accum: str = "f64") -> np.ndarray:
+    """GatedMLP.forward up to down_proj (python/picosgl/layers/mlp.py:43-46):
+    gate_up = gate_up_proj.forward(x) (materialised in dtype), then
+    silu_and_mul(gate_up)."""
+    return silu_and_mul(linear(x, w_gate_up, bias, dtype, accum), dtype)
+
+
 def all_reduce_sum(partials, dtype: str = "bf16") -> np.ndarray:
     """Sum of the ranks' tensors, rounded to dtype once.
 

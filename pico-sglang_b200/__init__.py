@@ -1,7 +1,8 @@
 """B200-native tensor-parallel linear path for pico-sglang.
 
-Drop-in replacements for the reference's TP linear layers, fused
-residual-add + RMSNorm and PyNCCL communicator, running hand-written
+Drop-in replacements for the reference's TP linear layers, gated MLP
+activation (fused into gate_up_proj), fused residual-add + RMSNorm and
+PyNCCL communicator, running hand-written
 sm_100a kernels from libpgb.so (C ABI: include/pgb.h).
 
 The directory name contains a hyphen, so import it with
@@ -10,7 +11,7 @@ The directory name contains a hyphen, so import it with
 
 from . import _lib, ops
 from ._lib import PGBError, PGBTimeout
-from .ops import col_gemm, fused_add_rmsnorm, rmsnorm, row_gemm_allreduce_addnorm
+from .ops import col_gemm, fused_add_rmsnorm, gate_up_silu, rmsnorm, row_gemm_allreduce_addnorm, silu_and_mul
 
 __all__ = [
     "PGBError",
@@ -18,7 +19,9 @@ __all__ = [
     "_lib",
     "col_gemm",
     "fused_add_rmsnorm",
+    "gate_up_silu",
     "ops",
     "rmsnorm",
     "row_gemm_allreduce_addnorm",
+    "silu_and_mul",
 ]

@@ -73,6 +73,12 @@ _SIGS: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
     ),
+    "pgb_gate_up_silu_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "pgb_gate_up_silu": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
+    ),
+    "pgb_silu_and_mul": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "pgb_row_gemm_allreduce_addnorm": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_int, c_int,

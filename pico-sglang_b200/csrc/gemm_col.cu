@@ -4,6 +4,13 @@
 // LinearTPImpl.forward (python/picosgl/layers/linear.py:23-27) for the
 // column-parallel layers LinearColParallelMerged / LinearColParallelPartitioned
 // (linear.py:45-73). No collective follows a column-parallel GEMM.
+//
+// Gated mode (GLU = true): the gate_up_proj GEMM with silu_and_mul in its
+// epilogue, out[T, I] = silu(x . Wg^T) * (x . Wu^T) for the merged weight
+// W = [Wg; Wu] of 2I rows, which is GatedMLP.forward's gate_up_proj.forward
+// followed by act_fn (python/picosgl/layers/mlp.py:43-46). The [T, 2I]
+// intermediate never leaves the SM.
+#include "activation.h"
 #include "gemm_f32.h"
 #include "gemm_plan.h"
 #include "gemm_sm100.cuh"
@@ -11,7 +18,7 @@
 
 namespace pgb {
 
-template <typename IO, int BN, bool SWAP, int STAGES>
+template <typename IO, int BN, bool SWAP, int STAGES, bool GLU>
 __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
     col_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     GemmShape g, IO* __restrict__ y, const IO* __restrict__ bias) {
@@ -77,9 +84,41 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
       if (tc.nctb > 1) {
         // Split tile: reduce-scatter with the tile's other CTAs through L2.
         const int N = g.N;
-        split_reduce_tile<IO, BN>(g, tc, c, tmem, acc, bias, [&](int t, int n0, uint4 piece) {
+        split_reduce_tile<IO, BN, GLU>(g, tc, c, tmem, acc, bias, [&](int t, int n0, uint4 piece) {
           *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
         });
+      } else if constexpr (GLU && !SWAP) {
+        // Lane = token t; columns [0, BN/2) are the gate and [BN/2, BN) the
+        // up values of output features q * BN/2 ... Each is rounded to IO
+        // (the reference materialises gate_up) before silu(gate) * up.
+        const int t = tc.p * kTileP + row;
+#pragma unroll 1
+        for (int col = 0; col < BN / 2; col += 32) {
+          float gv[32], uv[32];
+          epi_load_chunk<BN>(tmem, acc, col, gv);
+          epi_load_chunk<BN>(tmem, acc, BN / 2 + col, uv);
+          const int f0 = tc.q * (BN / 2) + col;
+          if (t < g.T) {
+            if (bias != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (f0 + j < g.N) {
+                  gv[j] += io_to_f32<IO>(bias[f0 + j]);
+                  uv[j] += io_to_f32<IO>(bias[g.N + f0 + j]);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              gv[j] = silu_f32_fast(io_to_f32<IO>(f32_to_io<IO>(gv[j]))) * io_to_f32<IO>(f32_to_io<IO>(uv[j]));
+            IO* dst = y + static_cast<size_t>(t) * g.N + f0;
+            if (f0 + 32 <= g.N) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = pack8<IO>(gv + 8 * j);
+            } else {
+              for (int j = 0; j < 32 && f0 + j < g.N; ++j) dst[j] = f32_to_io<IO>(gv[j]);
+            }
+          }
+        }
       } else {
 #pragma unroll 1
         for (int col = 0; col < BN; col += 32) {
@@ -88,17 +127,17 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
           if constexpr (SWAP) {
             // Lane = output feature n, columns = tokens: transpose through
             // shared memory and store 16-byte pieces of token rows.
-            const int n = tc.p * kTileP + row;
-            if (bias != nullptr && n < g.N) {
+            const int n = swap_weight_row<GLU>(g, tc.p, row);
+            if (bias != nullptr && n >= 0) {
               const float b = io_to_f32<IO>(bias[n]);
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += b;
             }
             const int N = g.N;
-            swap_epilogue_store<IO>(c.epi, v, tc.q * BN + col, 0, g.T, tc.p * kTileP, N,
-                                    [&](int t, int n0, uint4 piece) {
-                                      *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
-                                    });
+            swap_epilogue_store<IO, GLU>(c.epi, v, tc.q * BN + col, 0, g.T, tc.p * (GLU ? kTileP / 2 : kTileP), N,
+                                         [&](int t, int n0, uint4 piece) {
+                                           *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
+                                         });
           } else {
             // Lane = token t, columns = output features.
             const int t = tc.p * kTileP + row;
@@ -141,14 +180,15 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
 
 namespace {
 
-template <typename IO, int BN, bool SWAP>
+// N is the output width; the weight has N rows, or 2N ([gate; up]) when GLU.
+template <typename IO, int BN, bool SWAP, bool GLU>
 int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
                const void* bias, void* y, int T, int N, int K, uint8_t* ws, size_t ws_bytes,
                cudaStream_t stream) {
   constexpr int STAGES = gemm_stages<BN>();
   using L = GemmSmem<BN, STAGES>;
   static_assert(L::kBytes <= 232448, "shared memory budget");
-  auto kern = col_gemm_kernel<IO, BN, SWAP, STAGES>;
+  auto kern = col_gemm_kernel<IO, BN, SWAP, STAGES, GLU>;
   if (L::kBytes > dev.max_smem_optin)
     return set_error(PGB_ERR_UNSUPPORTED, "kernel needs %d B shared memory, device allows %d",
                      L::kBytes, dev.max_smem_optin);
@@ -158,14 +198,17 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
   if (col_workspace_bytes(p) > ws_bytes)
     return set_error(PGB_ERR_INVALID, "col_gemm: workspace of %zu bytes, %zu needed", ws_bytes,
                      col_workspace_bytes(p));
+  if (p.counter_bytes > kWsCounterBytes)
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d split tiles exceed the counter region",
+                     p.tiles - p.split_first);
 
   constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
   CUtensorMap tm_x, tm_w;
   int rc = make_tmap_2d_16bit(&tm_x, x, K, T, static_cast<uint64_t>(K) * 2, kBlockK,
                               SWAP ? BN : kTileP, kBf16);
   if (rc) return rc;
-  rc = make_tmap_2d_16bit(&tm_w, w, K, N, static_cast<uint64_t>(K) * 2, kBlockK,
-                          SWAP ? kTileP : BN, kBf16);
+  constexpr int kWRows = (SWAP ? kTileP : BN) / (GLU ? 2 : 1);  // weight box height
+  rc = make_tmap_2d_16bit(&tm_w, w, K, GLU ? 2 * N : N, static_cast<uint64_t>(K) * 2, kBlockK, kWRows, kBf16);
   if (rc) return rc;
 
   GemmShape g{};
@@ -183,8 +226,9 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
   g.nsplit = p.nsplit;
   g.status = reinterpret_cast<int*>(ws);
   g.ctr = reinterpret_cast<uint32_t*>(ws + kWsHeaderBytes);
-  g.xchg = reinterpret_cast<float*>(ws + kWsHeaderBytes + p.counter_bytes);
+  g.xchg = reinterpret_cast<float*>(ws + kWsHeaderBytes + kWsCounterBytes);
   g.wait_ns = 2000000000ull;  // 2 s: far beyond any legitimate pipeline stall
+  g.glu = GLU ? 1 : 0;
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(p.grid);
@@ -198,16 +242,16 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
                    static_cast<const IO*>(bias));
 }
 
-template <typename IO>
+template <typename IO, bool GLU>
 int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
                  const void* bias, void* y, int T, int N, int K, uint8_t* ws, size_t wsb,
                  cudaStream_t stream) {
-  if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+  if (!p.swap) return launch_col<IO, 256, false, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
   switch (p.bn) {
-    case 32: return launch_col<IO, 32, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-    case 64: return launch_col<IO, 64, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-    case 128: return launch_col<IO, 128, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-    case 256: return launch_col<IO, 256, true>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+    case 32: return launch_col<IO, 32, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+    case 64: return launch_col<IO, 64, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+    case 128: return launch_col<IO, 128, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
+    case 256: return launch_col<IO, 256, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
     default: return set_error(PGB_ERR_INVALID, "no kernel for tile width %d", p.bn);
   }
 }
@@ -261,8 +305,74 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
                      need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  if (dtype == PGB_BF16) return dispatch_col<__nv_bfloat16>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
-  return dispatch_col<__half>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
+  if (dtype == PGB_BF16)
+    return dispatch_col<__nv_bfloat16, false>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
+  return dispatch_col<__half, false>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
+}
+
+// ---------------------------------------------------------------------------
+// gate_up_proj GEMM with silu_and_mul in the epilogue.
+//
+// The work decomposition is that of the unfused [T, 2I] GEMM: a swap tile
+// pairs 64 gate rows with their 64 up rows, a prefill tile 128 with 128, so
+// plan_gemm(T, 2I, K) gives the same tile count, splits and scratch. The f32
+// check mode runs the f32 GEMM into the workspace and the activation kernel
+// after it.
+// ---------------------------------------------------------------------------
+
+namespace {
+size_t f32_gate_up_bytes(int T, int I) { return static_cast<size_t>(T) * 2u * static_cast<size_t>(I) * 4u; }
+}  // namespace
+
+extern "C" size_t pgb_gate_up_silu_workspace_size(int T, int I, int K, int dtype) {
+  using namespace pgb;
+  if (T <= 0 || I <= 0 || K <= 0) return kWsHeaderBytes;
+  if (dtype == PGB_F32) return kWsHeaderBytes + kWsCounterBytes + f32_gate_up_bytes(T, I);
+  const GemmPlan p = plan_gemm(T, 2 * I, K, sm_count_or_default(), SIZE_MAX);
+  return col_workspace_bytes(p);
+}
+
+extern "C" int pgb_gate_up_silu(const void* x, const void* w, const void* bias, void* out, int T, int I,
+                                int K, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace pgb;
+  if (T < 0 || I <= 0 || K <= 0 || I > (1 << 29))
+    return set_error(PGB_ERR_INVALID, "gate_up_silu: bad shape T=%d I=%d K=%d", T, I, K);
+  if (T == 0) return PGB_OK;
+  if (x == nullptr || w == nullptr || out == nullptr || workspace == nullptr)
+    return set_error(PGB_ERR_INVALID, "gate_up_silu: null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == PGB_F32) {
+    // f32 check mode: gate_up in the workspace's exchange area (the
+    // counters before it stay untouched), then the activation.
+    const size_t need = kWsHeaderBytes + kWsCounterBytes + f32_gate_up_bytes(T, I);
+    if (workspace_bytes < need)
+      return set_error(PGB_ERR_INVALID, "gate_up_silu: workspace of %zu bytes, %zu needed", workspace_bytes,
+                       need);
+    float* gu =
+        reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kWsHeaderBytes + kWsCounterBytes);
+    int rc = launch_gemm_f32(static_cast<const float*>(x), static_cast<const float*>(w),
+                             static_cast<const float*>(bias), gu, T, 2 * I, K, s);
+    if (rc) return rc;
+    return launch_silu_and_mul(gu, out, T, I, PGB_F32, s);
+  }
+  if (dtype != PGB_BF16 && dtype != PGB_F16)
+    return set_error(PGB_ERR_UNSUPPORTED, "gate_up_silu: dtype %d not supported", dtype);
+  if (K % 8 != 0 || I % 8 != 0)
+    return set_error(PGB_ERR_INVALID, "gate_up_silu: K=%d and I=%d must be multiples of 8", K, I);
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0u)
+    return set_error(PGB_ERR_INVALID, "gate_up_silu: output is not 16-byte aligned");
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  const GemmPlan p = plan_gemm(T, 2 * I, K, dev.sm_count, SIZE_MAX);
+  const size_t need = col_workspace_bytes(p);
+  if (workspace_bytes < need)
+    return set_error(PGB_ERR_INVALID, "gate_up_silu: workspace of %zu bytes, %zu needed", workspace_bytes,
+                     need);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  if (dtype == PGB_BF16)
+    return dispatch_col<__nv_bfloat16, true>(p, dev, x, w, bias, out, T, I, K, ws, workspace_bytes, s);
+  return dispatch_col<__half, true>(p, dev, x, w, bias, out, T, I, K, ws, workspace_bytes, s);
 }
 
 // ---------------------------------------------------------------------------
@@ -342,7 +452,7 @@ extern "C" int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bi
   // The status word and the split-tile counters must start at zero; the
   // exchange area behind them is written before it is read.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  PGB_CUDA_TRY(cudaMemsetAsync(scratch, 0, kWsHeaderBytes + p.counter_bytes, s));
+  PGB_CUDA_TRY(cudaMemsetAsync(scratch, 0, kWsHeaderBytes + kWsCounterBytes, s));
   return pgb_col_gemm(x, w, bias, y, T, N, K, dtype, scratch, PGB_NOALLOC_SCRATCH_BYTES, stream);
 }
 

@@ -29,13 +29,17 @@ struct GemmPlan {
 // The cheapest candidate under a measured-rate cost model is returned.
 GemmPlan plan_gemm(int T, int N, int K, int sms, size_t max_exchange_bytes);
 
-// Scratch layout used by the column GEMM: [status word, grid-barrier counters
-// | split-tile counters | exchange area]. The first
-// kWsHeaderBytes + counter_bytes bytes must be zero before the first call;
-// the kernel leaves them zero.
+// Scratch layout used by the column GEMM: [status word | split-tile counters
+// | exchange area]. The counter region has one size and place for every
+// plan, so the exchange area of one shape (f32 partials, left as they are)
+// never lies under the counters of another shape that shares the workspace.
+// The first kWsHeaderBytes + kWsCounterBytes bytes must be zero before the
+// first call; the kernels leave them zero. The exchange area is written
+// before it is read.
 constexpr size_t kWsHeaderBytes = 256;
+constexpr size_t kWsCounterBytes = 8192;  // 8 bytes per split tile: up to 1024 split tiles
 inline size_t col_workspace_bytes(const GemmPlan& p) {
-  return kWsHeaderBytes + p.counter_bytes + p.exchange_bytes;
+  return kWsHeaderBytes + kWsCounterBytes + p.exchange_bytes;
 }
 
 }  // namespace pgb

@@ -65,6 +65,7 @@ struct GemmShape {
   uint32_t* ctr;    // per split tile: {published, finished} counters, zero at rest
   int* status;      // device status word (first error wins)
   uint64_t wait_ns; // budget for every intra-kernel wait
+  int glu;          // gated mode: N = gated width I, the weight is [gate; up] of 2I rows
 };
 
 // One contiguous piece of a tile's reduction handled by this CTA.
@@ -134,6 +135,27 @@ __host__ __device__ __forceinline__ void split_cols(int V, int S, int r, int& c0
 // others' pieces) of its largest column run, 128 f32 per column.
 __host__ __device__ constexpr size_t split_recv_bytes(int BN, int S) {
   return static_cast<size_t>(S) * static_cast<size_t>((BN / 4 + S - 1) / S) * 4u * 128u * 4u;
+}
+
+// Weight tile of segment s, k-block kb, into dst (the A operand in the swap
+// orientation, B otherwise). In gated mode (g.glu) the weight is the merged
+// [gate; up] matrix of 2 * g.N rows (LinearColParallelMerged's layout,
+// python/picosgl/layers/linear.py:45-56) and a tile is two boxes of half
+// height: gate rows r0 .. and the up rows g.N + r0 .. of the same output
+// features, stacked. Both halves are whole 1024-byte swizzle atoms, so the
+// stacked boxes have the layout of one full-height box.
+template <int BN, bool SWAP>
+__device__ __forceinline__ void load_weight_tile(const GemmShape& g, const CUtensorMap* tm, uint64_t* bar,
+                                                 uint8_t* dst, int kb, const Seg& s, uint64_t hint) {
+  constexpr int kRows = SWAP ? kTileP : BN;
+  const int t = SWAP ? s.p : s.q;
+  if (!g.glu) {
+    tma_load_2d(tm, bar, dst, kb * kBlockK, t * kRows, hint);
+    return;
+  }
+  const int r0 = t * (kRows / 2);
+  tma_load_2d(tm, bar, dst, kb * kBlockK, r0, hint);
+  tma_load_2d(tm, bar, dst + (kRows / 2) * kBlockK * 2, kb * kBlockK, g.N + r0, hint);
 }
 
 template <int BN, int STAGES>
@@ -225,9 +247,9 @@ __device__ __forceinline__ int gemm_prefetch_weights(const GemmShape& g, const G
     for (int kb = s0.kb0; kb < s0.kb1 && pre < STAGES; ++kb, ++pre) {
       mbar_arrive_expect_tx(&c.full[pre], L::kStageBytes);
       if (SWAP)
-        tma_load_2d(tm_a, &c.full[pre], c.a + pre * L::kABytes, kb * kBlockK, s0.p * kTileP, hint_w);
+        load_weight_tile<BN, SWAP>(g, tm_a, &c.full[pre], c.a + pre * L::kABytes, kb, s0, hint_w);
       else
-        tma_load_2d(tm_b, &c.full[pre], c.b + pre * L::kBBytes, kb * kBlockK, s0.q * BN, hint_w);
+        load_weight_tile<BN, SWAP>(g, tm_b, &c.full[pre], c.b + pre * L::kBBytes, kb, s0, hint_w);
     }
   }
   return pre;
@@ -246,9 +268,9 @@ __device__ __forceinline__ void gemm_producer(const GemmShape& g, const GemmCtl&
   using L = GemmSmem<BN, STAGES>;
   auto load_w = [&](int stage, int kb, const Seg& s) {
     if (SWAP)
-      tma_load_2d(tm_a, &c.full[stage], c.a + stage * L::kABytes, kb * kBlockK, s.p * kTileP, hint_a);
+      load_weight_tile<BN, SWAP>(g, tm_a, &c.full[stage], c.a + stage * L::kABytes, kb, s, hint_a);
     else
-      tma_load_2d(tm_b, &c.full[stage], c.b + stage * L::kBBytes, kb * kBlockK, s.q * BN, hint_b);
+      load_weight_tile<BN, SWAP>(g, tm_b, &c.full[stage], c.b + stage * L::kBBytes, kb, s, hint_b);
   };
   auto load_x = [&](int stage, int kb, const Seg& s) {
     if (SWAP)
@@ -427,6 +449,43 @@ __device__ __forceinline__ void unpack8(uint4 u, float* v) {
   }
 }
 
+// SiLU in f32 as the reference's activation computes it: silu_and_mul
+// (python/picosgl/layers/activation.py:9-12) runs flashinfer's act_and_mul
+// kernel, which evaluates x / (1 + exp(-x)) with the fast exponential and
+// multiplies by the up value in f32.
+__device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + __expf(-x)); }
+
+// The same with the quotient from the fast reciprocal (__fdividef: at most
+// 2 ulp from the IEEE quotient for denominators up to 2^126, 0 beyond, where
+// the quotient is below 2^-100). The GEMM epilogues use it: the IEEE division
+// made the gated epilogue the longest part of a wide tile.
+__device__ __forceinline__ float silu_f32_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// out[e] = silu(gate[e]) * up[e] for 8 packed 16-bit values, rounded once.
+template <typename IO, bool FAST>
+__device__ __forceinline__ uint4 silu_mul8(uint4 gate, uint4 up) {
+  float gv[8], uv[8];
+  unpack8<IO>(gate, gv);
+  unpack8<IO>(up, uv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) gv[e] = (FAST ? silu_f32_fast(gv[e]) : silu_f32(gv[e])) * uv[e];
+  return pack8<IO>(gv);
+}
+
+// Row of the merged weight (and bias) that tile row `row` of swap-orientation
+// tile p holds, or -1 past the end. Gated mode: rows 0..63 are the gate rows
+// of output features p * 64 .., rows 64..127 the up rows of the same features.
+template <bool GLU>
+__device__ __forceinline__ int swap_weight_row(const GemmShape& g, int p, int row) {
+  if constexpr (GLU) {
+    const int f = p * (kTileP / 2) + (row & (kTileP / 2 - 1));
+    return f < g.N ? (row < kTileP / 2 ? f : g.N + f) : -1;
+  } else {
+    const int n = p * kTileP + row;
+    return n < g.N ? n : -1;
+  }
+}
+
 // Load 32 accumulator columns [col, col + 32) of accumulator acc.
 template <int BN>
 __device__ __forceinline__ void epi_load_chunk(uint32_t tmem, int acc, int col, float* v) {
@@ -441,8 +500,11 @@ __device__ __forceinline__ void epi_load_chunk(uint32_t tmem, int acc, int col, 
 // token t0 + j), j < 32. Stage the 32 x 128 block through shared memory so
 // it leaves as 16-byte pieces of token rows. emit(t, n0, piece) receives
 // 8 consecutive features [n0, n0 + 8) of token t, for tokens in
-// [t_lo, t_hi). All 128 epilogue threads call this together.
-template <typename IO, typename Emit>
+// [t_lo, t_hi) and n0 < N. All 128 epilogue threads call this together.
+// GLU: rows 0..63 hold gate and rows 64..127 up values of the 64 features
+// [n_base, n_base + 64); each staged value is rounded to IO (the reference
+// materialises gate_up in IO) and a piece is silu(gate) * up.
+template <typename IO, bool GLU = false, typename Emit>
 __device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* v, int t0, int t_lo, int t_hi,
                                                     int n_base, int N, Emit&& emit) {
   const int row = epi_row();
@@ -454,12 +516,26 @@ __device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* 
   }
   named_bar_sync(1, kEpiThreads);
   const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
+  if constexpr (GLU) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int idx = tid + k * kEpiThreads;  // 512 pieces: 32 tokens x 16 pieces
-    const int j = idx >> 4, piece = idx & 15;
-    const int t = t0 + j, n0 = n_base + piece * 8;
-    if (t >= t_lo && t < t_hi && n0 < N) emit(t, n0, *reinterpret_cast<const uint4*>(epi + j * kTileP + piece * 8));
+    for (int k = 0; k < 2; ++k) {
+      const int idx = tid + k * kEpiThreads;  // 256 pieces: 32 tokens x 8 pieces
+      const int j = idx >> 3, piece = idx & 7;
+      const int t = t0 + j, n0 = n_base + piece * 8;
+      const uint16_t* src = epi + j * kTileP + piece * 8;
+      if (t >= t_lo && t < t_hi && n0 < N)
+        emit(t, n0, silu_mul8<IO, true>(*reinterpret_cast<const uint4*>(src),
+                                        *reinterpret_cast<const uint4*>(src + kTileP / 2)));
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int idx = tid + k * kEpiThreads;  // 512 pieces: 32 tokens x 16 pieces
+      const int j = idx >> 4, piece = idx & 15;
+      const int t = t0 + j, n0 = n_base + piece * 8;
+      if (t >= t_lo && t < t_hi && n0 < N)
+        emit(t, n0, *reinterpret_cast<const uint4*>(epi + j * kTileP + piece * 8));
+    }
   }
 }
 
@@ -475,11 +551,12 @@ __device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* 
 //      pipeline ring, which is idle after its last MMA;
 //   3. sums its columns in split order (its own values were parked in its
 //      ring in step 1), adds the bias once, rounds and hands 16-byte pieces
-//      of token rows to emit(t, n0, uint4) through the shared staging tile;
+//      of token rows to emit(t, n0, uint4) through the shared staging tile
+//      (GLU: pieces of silu(gate) * up, see swap_epilogue_store);
 //   4. bumps the tile's second counter; the last CTA to finish resets both,
 //      so the counters are zero again for the next launch.
 // Returns false (and records an error) if a wait runs out.
-template <typename IO, int BN, typename Emit16>
+template <typename IO, int BN, bool GLU = false, typename Emit16>
 __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg& sg, const GemmCtl& c, uint32_t tmem,
                                                   int acc, const IO* bias, Emit16&& emit) {
   const int S = sg.nctb, j = sg.contrib, u = sg.tile - g.split_first;
@@ -564,8 +641,8 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
   //    memory only and branch-free: token indices past this CTA's run are
   //    clamped (those lanes of the staging tile are not emitted).
   if (ok && n_mine > 0) {
-    const int nf = sg.p * kTileP + row;
-    const float b = (bias != nullptr && nf < g.N) ? io_to_f32<IO>(bias[nf]) : 0.f;
+    const int nf = swap_weight_row<GLU>(g, sg.p, row);
+    const float b = (bias != nullptr && nf >= 0) ? io_to_f32<IO>(bias[nf]) : 0.f;
     const float* base = recv + row;
 #pragma unroll 1
     for (int c0 = 0; c0 < n_mine; c0 += 32) {
@@ -584,7 +661,8 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) v[jj] += b;
       if (tid == 0 && c0 == 0) trace(1015);
-      swap_epilogue_store<IO>(c.epi, v, t_base + my0 + c0, t_base + my0, t_base + my1, sg.p * kTileP, g.N, emit);
+      swap_epilogue_store<IO, GLU>(c.epi, v, t_base + my0 + c0, t_base + my0, t_base + my1,
+                                   sg.p * (GLU ? kTileP / 2 : kTileP), g.N, emit);
       if (tid == 0 && c0 == 0) trace(1016);
     }
   }

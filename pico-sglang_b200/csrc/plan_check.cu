@@ -107,6 +107,11 @@ extern "C" int pgb_check_work_plan(int T, int N, int K, int sms, int all_streamk
   if (p.counter_bytes < static_cast<size_t>(p.tiles - p.split_first) * 8u)
     return set_error(PGB_ERR_STATE, "counters need %d bytes, plan reserves %zu", (p.tiles - p.split_first) * 8,
                      p.counter_bytes);
+  // Counters live in a fixed region: the column workspace's, or the
+  // communicator's for the row kernel.
+  const size_t region = all_streamk ? kTileCounterBytes : kWsCounterBytes;
+  if (p.counter_bytes > region)
+    return set_error(PGB_ERR_STATE, "counters need %zu bytes, the region holds %zu", p.counter_bytes, region);
   // The gathered pieces must fit the smallest ring of this tile width.
   const size_t ring = static_cast<size_t>(gemm_stages_for(p.bn)) * (128u + p.bn) * 64u * 2u;
   if (p.nsplit > 1 && split_recv_bytes(p.bn, p.nsplit) > ring)

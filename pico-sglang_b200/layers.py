@@ -167,6 +167,42 @@ class LinearRowParallel(LinearTPImpl):
         return y.view(*x.shape[:-1], N)
 
 
+def silu_and_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """layers/activation.py:9-12: silu(x[..., :I]) * x[..., I:] on the libpgb kernel."""
+    return ops.silu_and_mul(x, out=out)
+
+
+class GatedMLP(BaseOP):
+    """layers/mlp.py:17-48 with the activation fused into gate_up_proj.
+
+    Same attributes (``gate_up_proj``, ``act_fn``, ``down_proj``) and shards.
+    While ``act_fn`` is this module's silu_and_mul, forward runs gate_up_proj
+    and the activation as one kernel (the [T, 2I] gate_up tensor is never
+    stored), then down_proj; an act_fn set to anything else runs unfused, in
+    the reference's order.
+    """
+
+    def __init__(self, hidden_size: int, intermediate_size: int, hidden_act: str):
+        self.gate_up_proj = LinearColParallelMerged(hidden_size, [intermediate_size, intermediate_size],
+                                                    has_bias=False)
+        if hidden_act == "silu":
+            self.act_fn = silu_and_mul
+        elif hidden_act == "gelu":
+            raise NotImplementedError("gelu_and_mul is not implemented by this library")
+        else:
+            raise ValueError(f"Unsupported activation function: {hidden_act}")
+        self.down_proj = LinearRowParallel(intermediate_size, hidden_size, has_bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.act_fn is silu_and_mul:
+            x2 = _flat2d(x).contiguous()
+            y = ops.gate_up_silu(x2, self.gate_up_proj.weight, self.gate_up_proj.bias)
+            y = y.view(*x.shape[:-1], y.shape[-1])
+        else:
+            y = self.act_fn(self.gate_up_proj.forward(x))
+        return self.down_proj.forward(y)
+
+
 class RMSNormFused(BaseOP):
     """norm.py:56-75 on libpgb kernels, aware of linked row-parallel producers."""
 

@@ -106,6 +106,55 @@ def col_gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
     return out
 
 
+def gate_up_silu(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(x . Wg^T) * (x . Wu^T) in one kernel; x [T, K], w = [Wg; Wu] of [2I, K].
+
+    GatedMLP.forward's gate_up_proj + silu_and_mul (python/picosgl/layers/mlp.py:43-46).
+    """
+    _require_cuda("x", x)
+    _require_cuda("weight", w)
+    if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1] or w.shape[0] % 2:
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} merged gate/up weight {tuple(w.shape)}")
+    if x.dtype != w.dtype:
+        raise TypeError(f"x {x.dtype} and weight {w.dtype} differ")
+    T, K = x.shape
+    I = w.shape[0] // 2
+    if bias is not None:
+        _require_cuda("bias", bias)
+        if bias.shape != (2 * I,) or bias.dtype != x.dtype:
+            raise ValueError("bias must be [2I] with the input dtype")
+    if out is None:
+        out = torch.empty((T, I), dtype=x.dtype, device=x.device)
+    else:
+        _require_cuda("out", out)
+        if out.shape != (T, I) or out.dtype != x.dtype:
+            raise ValueError("out must be [T, I] with the input dtype")
+    lib = _lib.load()
+    need = lib.pgb_gate_up_silu_workspace_size(T, I, K, dtype_code(x))
+    ws = WORKSPACES.get(x.device, need)
+    _lib.call("pgb_gate_up_silu", x.data_ptr(), w.data_ptr(), bias.data_ptr() if bias is not None else None,
+              out.data_ptr(), T, I, K, dtype_code(x), ws.data_ptr(), ws.numel(), _stream(x))
+    return out
+
+
+def silu_and_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(x[..., :I]) * x[..., I:] (python/picosgl/layers/activation.py:9-12)."""
+    _require_cuda("x", x)
+    if x.shape[-1] % 2:
+        raise ValueError(f"last dimension {x.shape[-1]} is not even")
+    I = x.shape[-1] // 2
+    T = x.numel() // max(x.shape[-1], 1)
+    if out is None:
+        out = torch.empty((*x.shape[:-1], I), dtype=x.dtype, device=x.device)
+    else:
+        _require_cuda("out", out)
+        if out.shape != (*x.shape[:-1], I) or out.dtype != x.dtype:
+            raise ValueError("out must be [..., I] with the input dtype")
+    _lib.call("pgb_silu_and_mul", x.data_ptr(), out.data_ptr(), T, I, dtype_code(x), _stream(x))
+    return out
+
+
 def row_gemm_allreduce_addnorm(comm, x_local: torch.Tensor, w_local: torch.Tensor,
                                residual: torch.Tensor | None, norm_w: torch.Tensor | None,
                                eps: float, out: torch.Tensor | None = None,

@@ -21,6 +21,14 @@ What it records:
   tp_small.npz  bf16 and f32 row-parallel results at TP 1/2/4 and the
              column-parallel merged / partitioned shards (with kv-head
              replication) produced by the reference's layers and loader.
+  mlp_small.npz  the reference's GatedMLP (python/picosgl/layers/mlp.py:17-48)
+             at TP 1/2, bf16 and f32: the gate_up tensor its forward hands to
+             act_fn and the activation's output. act_fn is silu_and_mul,
+             which runs FlashInfer on a GPU in the reference; here it is a
+             torch restatement of FlashInfer's act_and_mul kernel
+             (include/flashinfer/activation.cuh, silu from
+             flashinfer/jit/activation.py), checked against
+             torch.nn.functional.silu before it is used.
 """
 
 from __future__ import annotations
@@ -198,8 +206,65 @@ def make_tp_small():
     np.savez_compressed(HERE / "tp_small.npz", **data)
 
 
+def _torch_silu_and_mul(gate_up):
+    """Restatement of FlashInfer's act_and_mul kernel with silu: g / (1 + exp(-g)) * u in f32,
+    cast once to the input dtype."""
+    i = gate_up.shape[-1] // 2
+    g, u = gate_up[..., :i].float(), gate_up[..., i:].float()
+    return (g / (1.0 + torch.exp(-g)) * u).to(gate_up.dtype)
+
+
+def make_mlp_small():
+    (info, DistributedInfo, set_tp_info, DistributedCommunicator, DistributedImpl,
+     _, _, _, _shard_tensor) = _ref_imports()
+    from picosgl.layers.mlp import GatedMLP
+
+    class PassImpl(DistributedImpl):
+        def all_reduce(self, x):
+            return x
+
+        def all_gather(self, x):
+            raise AssertionError("not used")
+
+    g = torch.Generator().manual_seed(77)
+    H, I, T = 128, 192, 6
+    x = torch.randn(T, H, generator=g)
+    w_gate = torch.randn(I, H, generator=g) * 0.2
+    w_up = torch.randn(I, H, generator=g) * 0.1
+    w_down = torch.randn(H, I, generator=g) * 0.05
+    data = dict(x=x.numpy(), w_gate=w_gate.numpy(), w_up=w_up.numpy())
+    probe = torch.linspace(-30, 30, 2001)
+    ref = torch.nn.functional.silu(probe)
+    got = _torch_silu_and_mul(torch.cat([probe, torch.ones_like(probe)])[None])[0]
+    assert torch.allclose(got, ref, rtol=1e-6, atol=1e-7)
+    DistributedCommunicator.impl = PassImpl()
+    for dt_name, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+        for n in (1, 2):
+            for r in range(n):
+                _reset_tp(info, DistributedInfo, set_tp_info, r, n)
+                mlp = GatedMLP(H, I, "silu")
+                mlp.gate_up_proj.weight = torch.cat(
+                    [_shard_tensor("m.gate_proj.weight", w_gate, r, n, 1),
+                     _shard_tensor("m.up_proj.weight", w_up, r, n, 1)], 0).to(dt)
+                mlp.down_proj.weight = _shard_tensor("m.down_proj.weight", w_down, r, n, 1).to(dt)
+                seen = {}
+
+                def act(gate_up, out=None, seen=seen):
+                    seen["gate_up"] = gate_up.clone()
+                    seen["act"] = _torch_silu_and_mul(gate_up)
+                    return seen["act"]
+
+                mlp.act_fn = act
+                mlp.forward(x.to(dt))
+                data[f"gateup_{dt_name}_tp{n}_r{r}"] = seen["gate_up"].float().numpy()
+                data[f"act_{dt_name}_tp{n}_r{r}"] = seen["act"].float().numpy()
+    data["meta"] = np.array(f"H={H} I={I} T={T} seed=77 gate*0.2 up*0.1 down*0.05")
+    np.savez_compressed(HERE / "mlp_small.npz", **data)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
     make_tp_small()
+    make_mlp_small()
     make_cfg1()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))

@@ -36,6 +36,8 @@ SHAPES = [
     # (T, N, K): decode TP=1/8 qkv, gate_up; ragged tokens; tails in N and K
     (1, 6144, 4096),
     (8, 6144, 4096),
+    (1, 24576, 4096),  # gate_up: a full wave of whole tiles, then a split tail
+    (256, 24576, 4096),
     (32, 768, 4096),
     (33, 3072, 4096),
     (64, 1280, 5120),
@@ -88,3 +90,30 @@ def test_col_gemm_rejects_bad_shapes(pgb, cuda_device):
     w = torch.randn(16, 12, device=cuda_device).bfloat16()
     with pytest.raises(pgb.PGBError, match="multiples of 8"):
         pgb.col_gemm(x, w)
+
+
+def test_col_gemm_shapes_share_one_workspace(pgb, cuda_device):
+    """Calls of different shapes on one workspace, through the C ABI. The
+    first plans few split tiles (a small counter set) and leaves f32 partials
+    in its exchange area; the later ones plan more split tiles, so with a
+    plan-sized counter region their counters would lie where those partials
+    are. The counter region is fixed, so every call is exact."""
+    import ctypes
+
+    lib = pgb._lib.load()
+    shapes = [(32, 768, 4096), (1, 24576, 4096), (33, 3072, 4096), (128, 24576, 4096), (32, 768, 4096)]
+    need = max(lib.pgb_col_gemm_workspace_size(T, N, K) for T, N, K in shapes)
+    ws = torch.zeros(need, dtype=torch.uint8, device=cuda_device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for i, (T, N, K) in enumerate(shapes):
+        g = torch.Generator(device=cuda_device).manual_seed(300 + i)
+        x = torch.randn(T, K, device=cuda_device, generator=g).bfloat16()
+        w = (torch.randn(N, K, device=cuda_device, generator=g) * 0.02).bfloat16()
+        y = torch.empty(T, N, dtype=torch.bfloat16, device=cuda_device)
+        rc = lib.pgb_col_gemm(x.data_ptr(), w.data_ptr(), None, y.data_ptr(), T, N, K, 1, ws.data_ptr(),
+                              ctypes.c_size_t(need), stream)
+        assert rc == 0, lib.pgb_last_error()
+        torch.cuda.synchronize()
+        _check(y, _ref(x, w))
+    head = ws[:256 + 8192]
+    assert int(head.count_nonzero().item()) == 0, "status word and counters are left zeroed"

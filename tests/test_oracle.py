@@ -145,3 +145,57 @@ def test_tp_layer_step_sharded_equals_unsharded():
     four = oracle.tp_layer_step(h, a, m, res, wts, 1e-6, n=4, rank=2, dtype="f32")
     for k in ("x1", "r1", "x2", "r2"):
         np.testing.assert_allclose(four[k], one[k], rtol=1e-5, atol=1e-5)
+
+
+@pytest.fixture(scope="module")
+def mlp_small():
+    return dict(np.load(GOLD / "mlp_small.npz"))
+
+
+@pytest.mark.parametrize("n", [1, 2])
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_gated_mlp_activation_matches_reference(mlp_small, n, dt):
+    """The reference GatedMLP's gate_up (its merged shards) and its act_fn
+    output (mlp.py:43-46), recorded by tests/golden/make_golden.py."""
+    for r in range(n):
+        w_gu = oracle.col_shard_merged([mlp_small["w_gate"], mlp_small["w_up"]], r, n)
+        gu_ref = mlp_small[f"gateup_{dt}_tp{n}_r{r}"]
+        gu = oracle.linear(oracle.round_to(mlp_small["x"], dt), oracle.round_to(w_gu, dt), dtype=dt)
+        if dt == "f32":
+            assert np.abs(gu - gu_ref).max() <= 1e-5 * np.abs(gu_ref).max()
+        else:
+            # torch's CPU bf16 matmul rounds an f32 accumulation: at most one ulp apart.
+            ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(gu_ref), 1e-30))) - 7)
+            assert np.all(np.abs(gu - gu_ref) <= ulp)
+        act = oracle.silu_and_mul(gu_ref, dt)
+        act_ref = mlp_small[f"act_{dt}_tp{n}_r{r}"]
+        assert act.shape == (gu_ref.shape[0], gu_ref.shape[1] // 2)
+        if dt == "f32":
+            assert np.abs(act - act_ref).max() <= 1e-6 * np.abs(act_ref).max()
+        else:
+            ulp = 2.0 ** (np.floor(np.log2(np.maximum(np.abs(act_ref), 1e-30))) - 7)
+            assert np.all(np.abs(act - act_ref) <= ulp)
+            assert np.mean(act != act_ref) < 0.01
+
+
+def test_silu_and_mul_against_torch_silu():
+    """Independent pin: torch.nn.functional.silu times the up half, and the
+    limits silu(0) = 0, silu(x) -> x for large x, -> 0 for very negative x."""
+    x = np.linspace(-90, 90, 4001, dtype=np.float32)
+    gu = np.concatenate([x, np.ones_like(x)])[None]
+    got = oracle.silu_and_mul(gu, "f32")[0]
+    ref = torch.nn.functional.silu(torch.from_numpy(x)).numpy()
+    assert np.allclose(got, ref, rtol=2e-6, atol=1e-30)
+    edge = oracle.silu_and_mul(np.array([[0.0, 50.0, -200.0, 2.0, 3.0, 4.0]], np.float32), "f32")[0]
+    assert edge[0] == 0.0 and abs(edge[1] - 150.0) < 1e-4 and edge[2] == 0.0
+
+
+def test_gate_up_silu_ragged_and_empty():
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((3, 24)).astype(np.float32)
+    w = (rng.standard_normal((2 * 5, 24)) * 0.1).astype(np.float32)
+    y = oracle.gate_up_silu(x, w, dtype="f32")
+    gu = x.astype(np.float64) @ w.T.astype(np.float64)
+    ref = gu[:, :5] / (1 + np.exp(-gu[:, :5])) * gu[:, 5:]
+    assert np.allclose(y, ref, rtol=1e-5, atol=1e-6)
+    assert oracle.gate_up_silu(x[:0], w, dtype="bf16").shape == (0, 5)
