@@ -16,7 +16,9 @@ norm's output -> down_proj fused with the all-reduce and the next layer's
 input_layernorm. Attention and silu_and_mul are outside the step; their
 outputs are fixed synthetic activations. The gated MLP's front half
 (gate_up_proj + silu_and_mul, fused by pgb_gate_up_silu) is timed beside the
-step under `config.mlp_front_us`. L is chosen so the step's weights
+step under `config.mlp_front_us`, and the attention block's front (qkv_proj +
+RoPE + KV-cache store, fused by pgb_qkv_rope_store) under
+`config.attn_front_us`. L is chosen so the step's weights
 exceed 3x the 126 MB L2, so every layer streams its weights from HBM (no L2
 flush is needed). The step is captured once in a CUDA graph (as the
 reference's decode graphs, engine/graph.py:100-142) and replayed.
@@ -345,6 +347,7 @@ def run_ours(args) -> dict | None:
         del gg
     breakdown["gate_up"] = round(gu_us, 3)
     mlp_front = mlp_front_timings(args, pgb, layers, x1, stream, barrier, n_layers)
+    attn_front = attn_front_timings(args, pgb, L, layers, st.h, stream, barrier, n_layers, n, dev)
 
     # End to end through the public API: pinned host inputs copied in, the
     # captured layer stack replayed, the output and residual copied out.
@@ -414,6 +417,7 @@ def run_ours(args) -> dict | None:
                 "per_tokens": {str(k): v for k, v in per_t.items()},
                 "op_breakdown_us": breakdown,
                 "mlp_front_us": mlp_front,
+                "attn_front_us": attn_front,
                 "layer_roofline_us": head["roofline_us"],
                 "layer_frac_of_roofline": head["frac_of_roofline"],
             },
@@ -474,6 +478,68 @@ def mlp_front_timings(args, pgb, layers, x1, stream, barrier, n_layers) -> dict:
         def f(fn=fn):
             for lay in layers:
                 fn(lay)
+
+        with torch.cuda.stream(stream):
+            gg = capture(f, stream)
+            ms = time_graph(gg, stream, args.steps, args.warmup, barrier)
+        ms_t = torch.tensor([ms])
+        if dist_is_initialized():
+            torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+        out[name] = round(ms_t.item() * 1000.0 / args.steps / n_layers, 3)
+        del gg
+    return out
+
+
+def attn_front_timings(args, pgb, L, layers, h, stream, barrier, n_layers, n, dev) -> dict:
+    """The attention block's front, qkv_proj + RoPE + KV-cache store
+    (RotaryAttention.proj, python/picosgl/layers/attention.py:94-117, then
+    store_kv), per layer at the headline T, three ways: the fused kernel, this
+    library's GEMM then its standalone RoPE + store, and the reference's calls
+    (F.linear + flashinfer.apply_rope_with_cos_sin_cache_inplace + an index
+    store). Positions are random below 4096 (RoPE theta 1e6, config 5); each
+    layer writes its own [4096, kv heads, 128] caches at random slots."""
+    import torch.nn.functional as F
+
+    T = h.shape[0]
+    nq, nkv = NQ // n, max(NKV // n, 1)
+    table = L.get_rope(HD, HD, 4096, 1e6, None).cache_on(dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    pos = torch.randint(0, 4096, (T,), generator=g, device=dev, dtype=torch.int32)
+    loc = torch.randperm(4096, generator=g, device=dev)[:T].to(torch.int32)
+    caches = [(torch.zeros(4096, nkv, HD, device=dev, dtype=torch.bfloat16),
+               torch.zeros(4096, nkv, HD, device=dev, dtype=torch.bfloat16)) for _ in layers]
+
+    def fused(lay, kc, vc):
+        pgb.ops.qkv_rope_store(h, lay["qkv"].weight, pos, loc, table, nq, nkv, HD, kc, vc)
+
+    def unfused(lay, kc, vc):
+        pgb.ops.rope_store(pgb.col_gemm(h, lay["qkv"].weight), pos, loc, table, nq, nkv, HD, kc, vc)
+
+    ways = {"fused_qkv_rope_store": fused, "col_gemm_then_rope_store": unfused}
+    if args.library_baseline:
+        try:
+            import flashinfer
+
+            rope = flashinfer.apply_rope_with_cos_sin_cache_inplace
+            loc64 = loc.long()
+
+            def library(lay, kc, vc):
+                # The split views go to flashinfer strided, as RotaryEmbedding.forward
+                # reshapes them without a copy (python/picosgl/layers/rotary.py:40-45).
+                qkv = F.linear(h, lay["qkv"].weight)
+                q, k, v = qkv.split([nq * HD, nkv * HD, nkv * HD], dim=-1)
+                rope(pos, q, k, HD, table, is_neox=True)
+                kc[loc64] = k.view(T, nkv, HD)
+                vc[loc64] = v.view(T, nkv, HD)
+
+            ways["F.linear_flashinfer_rope_index_store"] = library
+        except Exception:  # pragma: no cover - flashinfer missing
+            pass
+    out = {"tokens": int(T), "q_heads": nq, "kv_heads": nkv}
+    for name, fn in ways.items():
+        def f(fn=fn):
+            for lay, (kc, vc) in zip(layers, caches):
+                fn(lay, kc, vc)
 
         with torch.cuda.stream(stream):
             gg = capture(f, stream)

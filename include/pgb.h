@@ -48,6 +48,12 @@ extern "C" {
 #define PGB_BF16 1
 #define PGB_F32 2
 
+/* Index element types (positions and KV-cache slots; the reference's engine
+ * uses int32, engine/engine.py:138,383-395, its store kernel takes either,
+ * csrc/jit/store.cu:25-28). */
+#define PGB_I32 3
+#define PGB_I64 4
+
 /* Reduction ops (csrc/src/pynccl.cu:44-47). Only sum is on the hot path. */
 #define PGB_OP_SUM 0
 
@@ -172,6 +178,50 @@ PGB_API int pgb_gate_up_silu(const void* x, const void* w, const void* bias, voi
  * Replaces silu_and_mul (python/picosgl/layers/activation.py:9-12) on a
  * materialised gate_up tensor. */
 PGB_API int pgb_silu_and_mul(const void* x, void* out, int T, int I, int dtype, void* stream);
+
+/* qkv_proj GEMM with RoPE and the KV-cache store in its epilogue:
+ *   qkv      = x[T, K] . w[N, K]^T (+ bias[N]), N = (nq + 2 nkv) hd, rounded to dtype
+ *   q_out[t] = rope(q heads of qkv[t], positions[t])                  [T, nq hd]
+ *   k_cache[out_loc[t]] = rope(k heads of qkv[t], positions[t])        rows of nkv hd
+ *   v_cache[out_loc[t]] = v heads of qkv[t]
+ * w is LinearColParallelPartitioned's local [q; k; v] weight
+ * (python/picosgl/layers/linear.py:59-73). RoPE is flashinfer's
+ * apply_rope_with_cos_sin_cache_inplace with is_neox = true as
+ * RotaryEmbedding.forward calls it (python/picosgl/layers/rotary.py:34-60):
+ * cos_sin_cache [max_position, rotary_dim] f32, cos in the first half; dims
+ * d < rotary_dim/2 pair with d + rotary_dim/2, in f32, rounded once; dims from
+ * rotary_dim on are not rotated. k_cache / v_cache are one layer's
+ * [cache_rows, nkv, hd] storage of MHAKVCachePool
+ * (python/picosgl/cache/kv/mha_pool.py:28-37). Replaces RotaryAttention.proj
+ * (python/picosgl/layers/attention.py:94-117) followed by the backend's
+ * store_kv (mha_pool.py:45-56 -> csrc/jit/store.cu:25-58). positions /
+ * out_loc: [T] of index_dtype (PGB_I32 or PGB_I64). A token whose position or
+ * slot is out of range is not written and sets the workspace's second int
+ * (byte offset 4, the index-error word) to 5; the caller reads and clears it. head_dim 64 or 128; rotary_dim a multiple of 64 up to
+ * head_dim; K % 8 == 0; q_out, caches and cos_sin_cache 16-byte aligned.
+ * dtype PGB_BF16 / PGB_F16, or PGB_F32 (check mode: f32 GEMM into the
+ * workspace, then pgb_rope_store). workspace: at least
+ * pgb_qkv_rope_store_workspace_size(...) bytes, zero-filled once; it may be
+ * the column GEMM's workspace. */
+PGB_API size_t pgb_qkv_rope_store_workspace_size(int T, int num_q_heads, int num_kv_heads, int head_dim,
+                                                 int K, int dtype);
+PGB_API int pgb_qkv_rope_store(const void* x, const void* w, const void* bias, int T, int K,
+                               int num_q_heads, int num_kv_heads, int head_dim, int rotary_dim,
+                               const void* positions, const void* out_loc, int index_dtype,
+                               const float* cos_sin_cache, int max_position, void* q_out, void* k_cache,
+                               void* v_cache, long long cache_rows, int dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* RoPE + KV-cache store from a materialised qkv [T, (nq + 2 nkv) hd] (same
+ * layout, arithmetic and limits as pgb_qkv_rope_store): flashinfer's
+ * apply_rope_with_cos_sin_cache_inplace (python/picosgl/layers/rotary.py:53-59)
+ * followed by store_cache (python/picosgl/kernel/store.py:37-51). status is a
+ * device int (the index-error word) set to 5 when a token is skipped for an
+ * out-of-range index. */
+PGB_API int pgb_rope_store(const void* qkv, int T, int num_q_heads, int num_kv_heads, int head_dim,
+                           int rotary_dim, const void* positions, const void* out_loc, int index_dtype,
+                           const float* cos_sin_cache, int max_position, void* q_out, void* k_cache,
+                           void* v_cache, long long cache_rows, int dtype, int* status, void* stream);
 
 /* Row-parallel GEMM fused with the all-reduce and the residual-add + RMSNorm
  * that consumes it:

@@ -3,6 +3,7 @@
 This package restates, in numpy, what the reference (dakingffo/pico-sglang)
 computes on the path the CUDA library replaces: the column-parallel and
 row-parallel linears, the gated MLP's silu_and_mul on the gate_up output,
+RoPE on the q and k heads with the KV-cache store,
 the sum all-reduce that follows a row-parallel linear, and the residual-add
 + RMSNorm that consumes it.
 
@@ -24,19 +25,26 @@ the installed flashinfer.fused_add_rmsnorm itself. silu_and_mul restates
 flashinfer's act_and_mul kernel the same way; it is pinned on the CPU to the
 reference's GatedMLP run with that restatement as its act_fn (mlp_small.npz)
 and to torch.nn.functional.silu, and on the GPU to flashinfer.silu_and_mul.
+apply_rope_neox restates flashinfer's rope kernel; its cos/sin table comes
+from the reference's own get_rope (rope_small.npz), the rotation is pinned to
+its defining properties on the CPU and to flashinfer's
+apply_rope_with_cos_sin_cache_inplace on the GPU.
 """
 
 from .tp_linear import (  # noqa: F401
     all_reduce_sum,
+    apply_rope_neox,
     col_shard_merged,
     col_shard_partitioned,
     fused_add_rmsnorm,
     gate_up_silu,
     linear,
+    qkv_rope_store,
     rmsnorm,
     round_to,
     row_parallel_addnorm,
     row_shard,
     silu_and_mul,
+    store_kv,
     tp_layer_step,
 )

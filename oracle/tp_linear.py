@@ -83,6 +83,59 @@ def gate_up_silu(x, w_gate_up, bias=None, dtype: str = "bf16", accum: str = "f64
     return silu_and_mul(linear(x, w_gate_up, bias, dtype, accum), dtype)
 
 
+def apply_rope_neox(x, positions, cos_sin_cache, head_dim: int, dtype: str = "bf16") -> np.ndarray:
+    """Rotate the heads of x [T, heads * head_dim] in place of the reference's
+    RotaryEmbedding.forward (python/picosgl/layers/rotary.py:34-60), which calls
+    flashinfer.apply_rope_with_cos_sin_cache_inplace with is_neox = True
+    (flashinfer 0.6.11, a third-party dependency not vendored in the reference).
+    Its kernel reads cos = table[pos][i], sin = table[pos][rd/2 + i] (float32)
+    and, for head dim i < rd/2 and its partner i + rd/2, computes in float32
+        x[i]        * cos - x[i + rd/2] * sin
+        x[i + rd/2] * cos + x[i]        * sin
+    rounded once to the tensor dtype; dims from rd on are unchanged.
+    """
+    a = np.asarray(x, np.float32)
+    T = a.shape[0]
+    h = a.reshape(T, -1, head_dim).copy()
+    table = np.asarray(cos_sin_cache, np.float32)
+    rd = table.shape[1]
+    half = rd // 2
+    rows = table[np.asarray(positions, np.int64)]
+    c, s = rows[:, None, :half], rows[:, None, half:]
+    x1, x2 = h[..., :half].copy(), h[..., half:rd].copy()
+    h[..., :half] = x1 * c - x2 * s
+    h[..., half:rd] = x2 * c + x1 * s
+    return round_to(h.reshape(T, -1), dtype)
+
+
+def store_kv(k_cache, v_cache, out_loc, k, v):
+    """k_cache[out_loc[t]] = k[t], v_cache[out_loc[t]] = v[t] on copies of the
+    caches ([slots, kv heads * head_dim] rows), as MHAKVCachePool.store_kv
+    (python/picosgl/cache/kv/mha_pool.py:45-56) does through store_cache
+    (python/picosgl/kernel/store.py:37-51, csrc/jit/store.cu:25-58: one warp
+    copies one token's row to its slot)."""
+    kc, vc = np.array(k_cache, copy=True), np.array(v_cache, copy=True)
+    loc = np.asarray(out_loc, np.int64)
+    kc.reshape(kc.shape[0], -1)[loc] = np.asarray(k).reshape(len(loc), -1)
+    vc.reshape(vc.shape[0], -1)[loc] = np.asarray(v).reshape(len(loc), -1)
+    return kc, vc
+
+
+def qkv_rope_store(x, w_qkv, bias, positions, out_loc, cos_sin_cache, num_q_heads: int, num_kv_heads: int,
+                   head_dim: int, k_cache, v_cache, dtype: str = "bf16", accum: str = "f64"):
+    """RotaryAttention.proj (python/picosgl/layers/attention.py:94-117) and the
+    backend's store_kv: qkv = qkv_proj(x) materialised in dtype, split into q,
+    k, v heads, q and k rotated, k and v stored at out_loc. Returns
+    (q [T, nq * hd], k_cache, v_cache)."""
+    qkv = linear(x, w_qkv, bias, dtype, accum)
+    qn, kvn = num_q_heads * head_dim, num_kv_heads * head_dim
+    q, k, v = qkv[:, :qn], qkv[:, qn:qn + kvn], qkv[:, qn + kvn:qn + 2 * kvn]
+    q = apply_rope_neox(q, positions, cos_sin_cache, head_dim, dtype)
+    k = apply_rope_neox(k, positions, cos_sin_cache, head_dim, dtype)
+    kc, vc = store_kv(k_cache, v_cache, out_loc, k, v)
+    return q, kc, vc
+
+
 def all_reduce_sum(partials, dtype: str = "bf16") -> np.ndarray:
     """Sum of the ranks' tensors, rounded to dtype once.
 

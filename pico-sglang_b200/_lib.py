@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import POINTER, c_char_p, c_float, c_int, c_size_t, c_uint8, c_uint64, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_longlong, c_size_t, c_uint8, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libpgb.so"
@@ -24,6 +24,8 @@ PGB_ERR_STATE = 5
 PGB_F16 = 0
 PGB_BF16 = 1
 PGB_F32 = 2
+PGB_I32 = 3
+PGB_I64 = 4
 PGB_OP_SUM = 0
 UID_BYTES = 128
 MAX_RANKS = 8
@@ -79,6 +81,17 @@ _SIGS: dict[str, tuple[object, list[object]]] = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p],
     ),
     "pgb_silu_and_mul": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "pgb_qkv_rope_store_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "pgb_qkv_rope_store": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int,
+         c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_longlong, c_int, c_void_p, c_size_t, c_void_p],
+    ),
+    "pgb_rope_store": (
+        c_int,
+        [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
+         c_void_p, c_void_p, c_longlong, c_int, c_void_p, c_void_p],
+    ),
     "pgb_row_gemm_allreduce_addnorm": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_int, c_int,

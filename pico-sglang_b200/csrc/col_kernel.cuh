@@ -1,0 +1,323 @@
+// col_kernel.cuh - the column-parallel GEMM kernel and its epilogue policies.
+//
+// y = x[T, K] . W^T on the tcgen05 core (gemm_sm100.cuh); what happens to the
+// f32 accumulators is the epilogue policy's business:
+//   EpiPlain : y[T, N] (+ bias), LinearTPImpl.forward for the column layers
+//              (python/picosgl/layers/linear.py:23-27, 45-73);
+//   EpiGlu   : silu(gate) * up for the merged [gate; up] weight, GatedMLP's
+//              gate_up_proj + act_fn (python/picosgl/layers/mlp.py:43-46);
+//   EpiRope  : (qkv_rope.cu) RoPE on q and k heads, q to its tensor and k, v
+//              into the paged KV cache (python/picosgl/layers/attention.py:94-117
+//              followed by MHAKVCachePool.store_kv).
+//
+// A policy is a trivially copyable struct passed to the kernel as a
+// __grid_constant__ parameter, with (all 128 epilogue threads call each
+// member together):
+//   static constexpr bool kGlu        weight tiles are gate / up halves
+//   static constexpr int kSmemBytes   shared memory the policy needs (c.extra)
+//   template <bool SWAP> void prepare(g, c)
+//                                     once, before the first accumulator is
+//                                     ready (the main loop is still running)
+//   float row_bias(g, p, row)         swap orientation: bias of tile row `row`
+//   void swap_chunk(g, c, v, p, t0, t_lo, t_hi)
+//                                     swap orientation: v[j] is tile row `row`
+//                                     of token t0 + j; store tokens [t_lo, t_hi)
+//   template <int BN> void nonswap_tile(g, tmem, acc, p, q)
+//                                     prefill orientation: the whole tile
+#pragma once
+
+#include "gemm_plan.h"
+#include "gemm_sm100.cuh"
+#include "host_common.h"
+
+namespace pgb {
+
+template <typename IO>
+struct EpiPlain {
+  static constexpr bool kGlu = false;
+  static constexpr int kSmemBytes = 0;
+  IO* y;
+  const IO* bias;
+
+  template <bool SWAP>
+  __device__ __forceinline__ void prepare(const GemmShape&, const GemmCtl&) const {}
+  __device__ __forceinline__ float row_bias(const GemmShape& g, int p, int row) const {
+    const int n = swap_weight_row<false>(g, p, row);
+    return (bias != nullptr && n >= 0) ? io_to_f32<IO>(bias[n]) : 0.f;
+  }
+  __device__ __forceinline__ void swap_chunk(const GemmShape& g, const GemmCtl& c, const float* v, int p, int t0,
+                                             int t_lo, int t_hi) const {
+    IO* out = y;
+    const int N = g.N;
+    swap_stage<IO>(c.epi, v);
+    swap_readout(c.epi, t0, t_lo, t_hi, p * kTileP, N, [&](int t, int n0, uint4 piece) {
+      *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * N + n0) = piece;
+    });
+  }
+  // Lane = token t, columns = output features.
+  template <int BN>
+  __device__ __forceinline__ void nonswap_tile(const GemmShape& g, uint32_t tmem, int acc, int p, int q) const {
+    const int t = p * kTileP + epi_row();
+#pragma unroll 1
+    for (int col = 0; col < BN; col += 32) {
+      float v[32];
+      epi_load_chunk<BN>(tmem, acc, col, v);
+      const int n0 = q * BN + col;
+      if (t < g.T) {
+        IO* dst = y + static_cast<size_t>(t) * g.N + n0;
+        if (bias != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < g.N) v[j] += io_to_f32<IO>(bias[n0 + j]);
+        }
+        if (n0 + 32 <= g.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = pack8<IO>(v + 8 * j);
+        } else {
+          for (int j = 0; j < 32 && n0 + j < g.N; ++j) dst[j] = f32_to_io<IO>(v[j]);
+        }
+      }
+    }
+  }
+};
+
+// Gated: g.N is the gated width I, the weight [gate; up] has 2I rows and the
+// bias (if any) 2I entries.
+template <typename IO>
+struct EpiGlu {
+  static constexpr bool kGlu = true;
+  static constexpr int kSmemBytes = 0;
+  IO* y;
+  const IO* bias;
+
+  template <bool SWAP>
+  __device__ __forceinline__ void prepare(const GemmShape&, const GemmCtl&) const {}
+  __device__ __forceinline__ float row_bias(const GemmShape& g, int p, int row) const {
+    const int n = swap_weight_row<true>(g, p, row);
+    return (bias != nullptr && n >= 0) ? io_to_f32<IO>(bias[n]) : 0.f;
+  }
+  __device__ __forceinline__ void swap_chunk(const GemmShape& g, const GemmCtl& c, const float* v, int p, int t0,
+                                             int t_lo, int t_hi) const {
+    IO* out = y;
+    const int N = g.N;
+    swap_stage<IO>(c.epi, v);
+    swap_readout_glu<IO>(c.epi, t0, t_lo, t_hi, p * (kTileP / 2), N, [&](int t, int n0, uint4 piece) {
+      *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * N + n0) = piece;
+    });
+  }
+  // Lane = token t; columns [0, BN/2) are the gate and [BN/2, BN) the up
+  // values of output features q * BN/2 ... Each is rounded to IO (the
+  // reference materialises gate_up) before silu(gate) * up.
+  template <int BN>
+  __device__ __forceinline__ void nonswap_tile(const GemmShape& g, uint32_t tmem, int acc, int p, int q) const {
+    const int t = p * kTileP + epi_row();
+#pragma unroll 1
+    for (int col = 0; col < BN / 2; col += 32) {
+      float gv[32], uv[32];
+      epi_load_chunk<BN>(tmem, acc, col, gv);
+      epi_load_chunk<BN>(tmem, acc, BN / 2 + col, uv);
+      const int f0 = q * (BN / 2) + col;
+      if (t < g.T) {
+        if (bias != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (f0 + j < g.N) {
+              gv[j] += io_to_f32<IO>(bias[f0 + j]);
+              uv[j] += io_to_f32<IO>(bias[g.N + f0 + j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          gv[j] = silu_f32_fast(io_to_f32<IO>(f32_to_io<IO>(gv[j]))) * io_to_f32<IO>(f32_to_io<IO>(uv[j]));
+        IO* dst = y + static_cast<size_t>(t) * g.N + f0;
+        if (f0 + 32 <= g.N) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = pack8<IO>(gv + 8 * j);
+        } else {
+          for (int j = 0; j < 32 && f0 + j < g.N; ++j) dst[j] = f32_to_io<IO>(gv[j]);
+        }
+      }
+    }
+  }
+};
+
+template <typename IO, int BN, bool SWAP, int STAGES, typename Epi>
+__global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
+    col_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                    GemmShape g, const __grid_constant__ Epi epi) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_pre;  // stages armed with weight tiles before pdl_wait()
+  GemmCtl c = gemm_carve_smem<BN, STAGES, Epi::kSmemBytes>(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    trace(1000);
+    tma_prefetch_desc(&tm_a);  // descriptor fetch overlaps barrier set-up
+    tma_prefetch_desc(&tm_b);
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&c.full[i], 1);
+      mbar_init(&c.empty[i], 1);
+    }
+    mbar_init(&c.acc_full[0], 1);
+    mbar_init(&c.acc_full[1], 1);
+    mbar_init(&c.acc_empty[0], kEpiThreads);
+    mbar_init(&c.acc_empty[1], kEpiThreads);
+    mbar_init(c.drain, 1);
+    mbar_init(c.xchg, 1);
+    *c.abort = 0;
+    fence_mbar_init();
+    trace(1005);
+    s_pre = gemm_prefetch_weights<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b,
+                                                   SWAP ? l2_policy_evict_first() : l2_policy_evict_last());
+    trace(1006);
+  }
+  if (warp == 1) {
+    tmem_alloc(c.tmem_base, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint64_t hw = l2_policy_evict_first();
+      const uint64_t hx = l2_policy_evict_last();
+      gemm_producer<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b, SWAP ? hw : hx, SWAP ? hx : hw, s_pre, [] {});
+    }
+  } else if (warp == 1) {
+    if (lane == 0) gemm_mma<BN, STAGES>(g, c, umma_idesc_f16(kTileP, BN, std::is_same<IO, __nv_bfloat16>::value));
+  } else {
+    pdl_wait();  // outputs (and the exchange area) may still be read by the previous kernel
+    epi.template prepare<SWAP>(g, c);
+    const uint32_t tmem = *c.tmem_base;
+    const int row = epi_row();
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    SegIter it(g);
+    Seg tc;
+    while (it.next(g, tc)) {
+      if (!mbar_wait(&c.acc_full[acc], acc_phase, g.wait_ns, c.abort)) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+        break;
+      }
+      tc_fence_after();
+      if (tc.nctb > 1) {
+        // Split tile: reduce-scatter with the tile's other CTAs through L2.
+        split_reduce_tile<BN>(g, tc, c, tmem, acc, epi.row_bias(g, tc.p, row),
+                              [&](const float* v, int t0, int t_lo, int t_hi) {
+                                epi.swap_chunk(g, c, v, tc.p, t0, t_lo, t_hi);
+                              });
+      } else if constexpr (SWAP) {
+        // Lane = tile row (output feature), columns = tokens.
+        const float b = epi.row_bias(g, tc.p, row);
+#pragma unroll 1
+        for (int col = 0; col < BN; col += 32) {
+          float v[32];
+          epi_load_chunk<BN>(tmem, acc, col, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += b;
+          epi.swap_chunk(g, c, v, tc.p, tc.q * BN + col, 0, g.T);
+        }
+      } else {
+        epi.template nonswap_tile<BN>(g, tmem, acc, tc.p, tc.q);
+      }
+      tc_fence_before();
+      mbar_arrive(&c.acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(*c.tmem_base, 2 * BN);
+  }
+  if (threadIdx.x == 0) trace(1001);
+}
+
+// Launch one column kernel. N is the output width g.N; the weight has N rows,
+// or 2N ([gate; up]) for a gated policy. ws is the column workspace
+// ([status | counters | exchange], col_workspace_bytes).
+template <typename IO, int BN, bool SWAP, typename Epi>
+int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
+               uint8_t* ws, size_t ws_bytes, cudaStream_t stream, const Epi& epi) {
+  constexpr int STAGES = gemm_stages<BN>();
+  using L = GemmSmem<BN, STAGES, Epi::kSmemBytes>;
+  static_assert(L::kBytes <= 232448, "shared memory budget");
+  static_assert(gemm_ctas_per_sm(BN) == 1 || 2 * (L::kBytes + 1024) <= 233472, "two CTAs per SM");
+  auto kern = col_gemm_kernel<IO, BN, SWAP, STAGES, Epi>;
+  if (L::kBytes > dev.max_smem_optin)
+    return set_error(PGB_ERR_UNSUPPORTED, "kernel needs %d B shared memory, device allows %d", L::kBytes,
+                     dev.max_smem_optin);
+  PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  if (p.nsplit > 1 && split_recv_bytes(BN, p.nsplit) > static_cast<size_t>(STAGES) * L::kStageBytes)
+    return set_error(PGB_ERR_STATE, "col_gemm: split of %d does not fit the pipeline ring", p.nsplit);
+  if (col_workspace_bytes(p) > ws_bytes)
+    return set_error(PGB_ERR_INVALID, "col_gemm: workspace of %zu bytes, %zu needed", ws_bytes,
+                     col_workspace_bytes(p));
+  if (p.counter_bytes > kWsCounterBytes)
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d split tiles exceed the counter region",
+                     p.tiles - p.split_first);
+
+  constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
+  CUtensorMap tm_x, tm_w;
+  int rc = make_tmap_2d_16bit(&tm_x, x, K, T, static_cast<uint64_t>(K) * 2, kBlockK, SWAP ? BN : kTileP, kBf16);
+  if (rc) return rc;
+  constexpr int kWRows = (SWAP ? kTileP : BN) / (Epi::kGlu ? 2 : 1);  // weight box height
+  rc = make_tmap_2d_16bit(&tm_w, w, K, Epi::kGlu ? 2 * N : N, static_cast<uint64_t>(K) * 2, kBlockK, kWRows,
+                          kBf16);
+  if (rc) return rc;
+
+  GemmShape g{};
+  g.T = T;
+  g.N = N;
+  g.K = K;
+  g.kblocks = p.kblocks;
+  g.p_tiles = p.p_tiles;
+  g.q_tiles = p.q_tiles;
+  g.tiles = p.tiles;
+  g.dp_rounds = p.dp_rounds;
+  g.split_first = p.split_first;
+  g.grid = p.grid;
+  g.split_ctas = p.split_ctas;
+  g.nsplit = p.nsplit;
+  g.status = reinterpret_cast<int*>(ws);
+  g.ctr = reinterpret_cast<uint32_t*>(ws + kWsHeaderBytes);
+  g.xchg = reinterpret_cast<float*>(ws + kWsHeaderBytes + kWsCounterBytes);
+  g.wait_ns = 2000000000ull;  // 2 s: far beyond any legitimate pipeline stall
+  g.glu = Epi::kGlu ? 1 : 0;
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  const CUtensorMap& ta = SWAP ? tm_w : tm_x;
+  const CUtensorMap& tb = SWAP ? tm_x : tm_w;
+  // The CTAs of a split tile wait for each other: cooperative launch.
+  return launch_ex(cfg, /*cooperative=*/p.split_ctas > 0, 1, kern, ta, tb, g, epi);
+}
+
+// The tile width the plan picked, for one policy.
+template <typename IO, typename Epi>
+int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
+                 uint8_t* ws, size_t wsb, cudaStream_t stream, const Epi& epi) {
+  if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
+  switch (p.bn) {
+    case 32: return launch_col<IO, 32, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
+    case 64: return launch_col<IO, 64, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
+    case 128: return launch_col<IO, 128, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
+    case 256: return launch_col<IO, 256, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
+    default: return set_error(PGB_ERR_INVALID, "no kernel for tile width %d", p.bn);
+  }
+}
+
+}  // namespace pgb

@@ -5,256 +5,18 @@
 // column-parallel layers LinearColParallelMerged / LinearColParallelPartitioned
 // (linear.py:45-73). No collective follows a column-parallel GEMM.
 //
-// Gated mode (GLU = true): the gate_up_proj GEMM with silu_and_mul in its
+// Gated mode (EpiGlu): the gate_up_proj GEMM with silu_and_mul in its
 // epilogue, out[T, I] = silu(x . Wg^T) * (x . Wu^T) for the merged weight
 // W = [Wg; Wu] of 2I rows, which is GatedMLP.forward's gate_up_proj.forward
 // followed by act_fn (python/picosgl/layers/mlp.py:43-46). The [T, 2I]
 // intermediate never leaves the SM.
 #include "activation.h"
+#include "col_kernel.cuh"
 #include "gemm_f32.h"
-#include "gemm_plan.h"
-#include "gemm_sm100.cuh"
-#include "host_common.h"
 
 namespace pgb {
 
-template <typename IO, int BN, bool SWAP, int STAGES, bool GLU>
-__global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
-    col_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                    GemmShape g, IO* __restrict__ y, const IO* __restrict__ bias) {
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ int s_pre;  // stages armed with weight tiles before pdl_wait()
-  GemmCtl c = gemm_carve_smem<BN, STAGES>(smem_raw);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    trace(1000);
-    tma_prefetch_desc(&tm_a);  // descriptor fetch overlaps barrier set-up
-    tma_prefetch_desc(&tm_b);
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&c.full[i], 1);
-      mbar_init(&c.empty[i], 1);
-    }
-    mbar_init(&c.acc_full[0], 1);
-    mbar_init(&c.acc_full[1], 1);
-    mbar_init(&c.acc_empty[0], kEpiThreads);
-    mbar_init(&c.acc_empty[1], kEpiThreads);
-    mbar_init(c.drain, 1);
-    mbar_init(c.xchg, 1);
-    *c.abort = 0;
-    fence_mbar_init();
-    trace(1005);
-    s_pre = gemm_prefetch_weights<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b,
-                                                   SWAP ? l2_policy_evict_first() : l2_policy_evict_last());
-    trace(1006);
-  }
-  if (warp == 1) {
-    tmem_alloc(c.tmem_base, 2 * BN);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (threadIdx.x == 0) pdl_launch_dependents();
-
-  if (warp == 0) {
-    if (lane == 0) {
-      const uint64_t hw = l2_policy_evict_first();
-      const uint64_t hx = l2_policy_evict_last();
-      gemm_producer<BN, STAGES, SWAP>(g, c, &tm_a, &tm_b, SWAP ? hw : hx, SWAP ? hx : hw, s_pre, [] {});
-    }
-  } else if (warp == 1) {
-    if (lane == 0) gemm_mma<BN, STAGES>(g, c, umma_idesc_f16(kTileP, BN, std::is_same<IO, __nv_bfloat16>::value));
-  } else {
-    pdl_wait();  // outputs (and the exchange area) may still be read by the previous kernel
-    const uint32_t tmem = *c.tmem_base;
-    const int row = epi_row();
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    SegIter it(g);
-    Seg tc;
-    while (it.next(g, tc)) {
-      if (!mbar_wait(&c.acc_full[acc], acc_phase, g.wait_ns, c.abort)) {
-        record_error(g.status, kDevTimeoutPipeline);
-        *reinterpret_cast<volatile int*>(c.abort) = 1;
-        break;
-      }
-      tc_fence_after();
-      if (tc.nctb > 1) {
-        // Split tile: reduce-scatter with the tile's other CTAs through L2.
-        const int N = g.N;
-        split_reduce_tile<IO, BN, GLU>(g, tc, c, tmem, acc, bias, [&](int t, int n0, uint4 piece) {
-          *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
-        });
-      } else if constexpr (GLU && !SWAP) {
-        // Lane = token t; columns [0, BN/2) are the gate and [BN/2, BN) the
-        // up values of output features q * BN/2 ... Each is rounded to IO
-        // (the reference materialises gate_up) before silu(gate) * up.
-        const int t = tc.p * kTileP + row;
-#pragma unroll 1
-        for (int col = 0; col < BN / 2; col += 32) {
-          float gv[32], uv[32];
-          epi_load_chunk<BN>(tmem, acc, col, gv);
-          epi_load_chunk<BN>(tmem, acc, BN / 2 + col, uv);
-          const int f0 = tc.q * (BN / 2) + col;
-          if (t < g.T) {
-            if (bias != nullptr) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (f0 + j < g.N) {
-                  gv[j] += io_to_f32<IO>(bias[f0 + j]);
-                  uv[j] += io_to_f32<IO>(bias[g.N + f0 + j]);
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              gv[j] = silu_f32_fast(io_to_f32<IO>(f32_to_io<IO>(gv[j]))) * io_to_f32<IO>(f32_to_io<IO>(uv[j]));
-            IO* dst = y + static_cast<size_t>(t) * g.N + f0;
-            if (f0 + 32 <= g.N) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = pack8<IO>(gv + 8 * j);
-            } else {
-              for (int j = 0; j < 32 && f0 + j < g.N; ++j) dst[j] = f32_to_io<IO>(gv[j]);
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int col = 0; col < BN; col += 32) {
-          float v[32];
-          epi_load_chunk<BN>(tmem, acc, col, v);
-          if constexpr (SWAP) {
-            // Lane = output feature n, columns = tokens: transpose through
-            // shared memory and store 16-byte pieces of token rows.
-            const int n = swap_weight_row<GLU>(g, tc.p, row);
-            if (bias != nullptr && n >= 0) {
-              const float b = io_to_f32<IO>(bias[n]);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += b;
-            }
-            const int N = g.N;
-            swap_epilogue_store<IO, GLU>(c.epi, v, tc.q * BN + col, 0, g.T, tc.p * (GLU ? kTileP / 2 : kTileP), N,
-                                         [&](int t, int n0, uint4 piece) {
-                                           *reinterpret_cast<uint4*>(y + static_cast<size_t>(t) * N + n0) = piece;
-                                         });
-          } else {
-            // Lane = token t, columns = output features.
-            const int t = tc.p * kTileP + row;
-            const int n0 = tc.q * BN + col;
-            if (t < g.T) {
-              IO* dst = y + static_cast<size_t>(t) * g.N + n0;
-              if (bias != nullptr) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (n0 + j < g.N) v[j] += io_to_f32<IO>(bias[n0 + j]);
-              }
-              if (n0 + 32 <= g.N) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  reinterpret_cast<uint4*>(dst)[j] = pack8<IO>(v + 8 * j);
-              } else {
-                for (int j = 0; j < 32 && n0 + j < g.N; ++j) dst[j] = f32_to_io<IO>(v[j]);
-              }
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&c.acc_empty[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(*c.tmem_base, 2 * BN);
-  }
-  if (threadIdx.x == 0) trace(1001);
-}
-
 namespace {
-
-// N is the output width; the weight has N rows, or 2N ([gate; up]) when GLU.
-template <typename IO, int BN, bool SWAP, bool GLU>
-int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
-               const void* bias, void* y, int T, int N, int K, uint8_t* ws, size_t ws_bytes,
-               cudaStream_t stream) {
-  constexpr int STAGES = gemm_stages<BN>();
-  using L = GemmSmem<BN, STAGES>;
-  static_assert(L::kBytes <= 232448, "shared memory budget");
-  auto kern = col_gemm_kernel<IO, BN, SWAP, STAGES, GLU>;
-  if (L::kBytes > dev.max_smem_optin)
-    return set_error(PGB_ERR_UNSUPPORTED, "kernel needs %d B shared memory, device allows %d",
-                     L::kBytes, dev.max_smem_optin);
-  PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
-  if (p.nsplit > 1 && split_recv_bytes(BN, p.nsplit) > static_cast<size_t>(STAGES) * L::kStageBytes)
-    return set_error(PGB_ERR_STATE, "col_gemm: split of %d does not fit the pipeline ring", p.nsplit);
-  if (col_workspace_bytes(p) > ws_bytes)
-    return set_error(PGB_ERR_INVALID, "col_gemm: workspace of %zu bytes, %zu needed", ws_bytes,
-                     col_workspace_bytes(p));
-  if (p.counter_bytes > kWsCounterBytes)
-    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d split tiles exceed the counter region",
-                     p.tiles - p.split_first);
-
-  constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
-  CUtensorMap tm_x, tm_w;
-  int rc = make_tmap_2d_16bit(&tm_x, x, K, T, static_cast<uint64_t>(K) * 2, kBlockK,
-                              SWAP ? BN : kTileP, kBf16);
-  if (rc) return rc;
-  constexpr int kWRows = (SWAP ? kTileP : BN) / (GLU ? 2 : 1);  // weight box height
-  rc = make_tmap_2d_16bit(&tm_w, w, K, GLU ? 2 * N : N, static_cast<uint64_t>(K) * 2, kBlockK, kWRows, kBf16);
-  if (rc) return rc;
-
-  GemmShape g{};
-  g.T = T;
-  g.N = N;
-  g.K = K;
-  g.kblocks = p.kblocks;
-  g.p_tiles = p.p_tiles;
-  g.q_tiles = p.q_tiles;
-  g.tiles = p.tiles;
-  g.dp_rounds = p.dp_rounds;
-  g.split_first = p.split_first;
-  g.grid = p.grid;
-  g.split_ctas = p.split_ctas;
-  g.nsplit = p.nsplit;
-  g.status = reinterpret_cast<int*>(ws);
-  g.ctr = reinterpret_cast<uint32_t*>(ws + kWsHeaderBytes);
-  g.xchg = reinterpret_cast<float*>(ws + kWsHeaderBytes + kWsCounterBytes);
-  g.wait_ns = 2000000000ull;  // 2 s: far beyond any legitimate pipeline stall
-  g.glu = GLU ? 1 : 0;
-
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(p.grid);
-  cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = L::kBytes;
-  cfg.stream = stream;
-  const CUtensorMap& ta = SWAP ? tm_w : tm_x;
-  const CUtensorMap& tb = SWAP ? tm_x : tm_w;
-  // The CTAs of a split tile wait for each other: cooperative launch.
-  return launch_ex(cfg, /*cooperative=*/p.split_ctas > 0, 1, kern, ta, tb, g, static_cast<IO*>(y),
-                   static_cast<const IO*>(bias));
-}
-
-template <typename IO, bool GLU>
-int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w,
-                 const void* bias, void* y, int T, int N, int K, uint8_t* ws, size_t wsb,
-                 cudaStream_t stream) {
-  if (!p.swap) return launch_col<IO, 256, false, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-  switch (p.bn) {
-    case 32: return launch_col<IO, 32, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-    case 64: return launch_col<IO, 64, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-    case 128: return launch_col<IO, 128, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-    case 256: return launch_col<IO, 256, true, GLU>(p, dev, x, w, bias, y, T, N, K, ws, wsb, stream);
-    default: return set_error(PGB_ERR_INVALID, "no kernel for tile width %d", p.bn);
-  }
-}
 
 int sm_count_or_default() {
   DeviceInfo d;
@@ -306,8 +68,11 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (dtype == PGB_BF16)
-    return dispatch_col<__nv_bfloat16, false>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
-  return dispatch_col<__half, false>(p, dev, x, w, bias, y, T, N, K, ws, workspace_bytes, s);
+    return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, N, K, ws, workspace_bytes, s,
+                                       EpiPlain<__nv_bfloat16>{static_cast<__nv_bfloat16*>(y),
+                                                               static_cast<const __nv_bfloat16*>(bias)});
+  return dispatch_col<__half>(p, dev, x, w, T, N, K, ws, workspace_bytes, s,
+                              EpiPlain<__half>{static_cast<__half*>(y), static_cast<const __half*>(bias)});
 }
 
 // ---------------------------------------------------------------------------
@@ -371,8 +136,11 @@ extern "C" int pgb_gate_up_silu(const void* x, const void* w, const void* bias, 
                      need);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   if (dtype == PGB_BF16)
-    return dispatch_col<__nv_bfloat16, true>(p, dev, x, w, bias, out, T, I, K, ws, workspace_bytes, s);
-  return dispatch_col<__half, true>(p, dev, x, w, bias, out, T, I, K, ws, workspace_bytes, s);
+    return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, I, K, ws, workspace_bytes, s,
+                                       EpiGlu<__nv_bfloat16>{static_cast<__nv_bfloat16*>(out),
+                                                             static_cast<const __nv_bfloat16*>(bias)});
+  return dispatch_col<__half>(p, dev, x, w, T, I, K, ws, workspace_bytes, s,
+                              EpiGlu<__half>{static_cast<__half*>(out), static_cast<const __half*>(bias)});
 }
 
 // ---------------------------------------------------------------------------

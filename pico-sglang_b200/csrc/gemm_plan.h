@@ -37,6 +37,7 @@ GemmPlan plan_gemm(int T, int N, int K, int sms, size_t max_exchange_bytes);
 // first call; the kernels leave them zero. The exchange area is written
 // before it is read.
 constexpr size_t kWsHeaderBytes = 256;
+constexpr size_t kWsIndexErrorOffset = 4;  // second int of the header: RoPE index errors (no wait polls it)
 constexpr size_t kWsCounterBytes = 8192;  // 8 bytes per split tile: up to 1024 split tiles
 inline size_t col_workspace_bytes(const GemmPlan& p) {
   return kWsHeaderBytes + kWsCounterBytes + p.exchange_bytes;

@@ -158,20 +158,22 @@ __device__ __forceinline__ void load_weight_tile(const GemmShape& g, const CUten
   tma_load_2d(tm, bar, dst + (kRows / 2) * kBlockK * 2, kb * kBlockK, g.N + r0, hint);
 }
 
-template <int BN, int STAGES>
+// EXTRA: bytes of an epilogue-policy region after the barriers (0: none).
+template <int BN, int STAGES, int EXTRA = 0>
 struct GemmSmem {
   static constexpr int kABytes = kTileP * kBlockK * 2;  // 16 KB
   static constexpr int kBBytes = BN * kBlockK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;  // two accumulators
-  // Layout (from a 1024-byte aligned base): A ring, B ring, barriers.
+  // Layout (from a 1024-byte aligned base): A ring, B ring, barriers, extra.
   static constexpr int kOffA = 0;
   static constexpr int kOffB = STAGES * kABytes;
   static constexpr int kOffEpi = kOffB + STAGES * kBBytes;
   static constexpr int kEpiBytes = 32 * kTileP * 2;  // 32 tokens x 128 features, 16-bit
   static constexpr int kOffBar = kOffEpi + kEpiBytes;
   static constexpr int kBarBytes = 8 * (2 * STAGES + 6) + 64;
-  static constexpr int kBytes = kOffBar + kBarBytes + 1024;  // + alignment slack
+  static constexpr int kOffExtra = kOffBar + kBarBytes;
+  static constexpr int kBytes = kOffExtra + EXTRA + 1024;  // + alignment slack
 };
 
 // CTAs per SM a GEMM kernel of tile width BN is built for. Narrow decode
@@ -206,11 +208,12 @@ struct GemmCtl {
   uint8_t* b;
   uint16_t* epi;  // [32][128] staging tile of the swap-orientation epilogue
   uint64_t* xchg; // split tiles: the others' pieces have landed in the ring
+  uint8_t* extra; // the epilogue policy's region (GemmSmem EXTRA bytes)
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EXTRA = 0>
 __device__ __forceinline__ GemmCtl gemm_carve_smem(uint8_t* raw) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, EXTRA>;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   GemmCtl c;
@@ -227,6 +230,7 @@ __device__ __forceinline__ GemmCtl gemm_carve_smem(uint8_t* raw) {
   c.tmem_base = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 6);
   c.abort = reinterpret_cast<int*>(c.tmem_base + 1);
   c.flag = c.abort + 1;
+  c.extra = base + L::kOffExtra;
   return c;
 }
 
@@ -496,17 +500,12 @@ __device__ __forceinline__ void epi_load_chunk(uint32_t tmem, int acc, int col, 
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// Swap orientation: this thread holds v[j] = out(feature p*128 + row,
-// token t0 + j), j < 32. Stage the 32 x 128 block through shared memory so
-// it leaves as 16-byte pieces of token rows. emit(t, n0, piece) receives
-// 8 consecutive features [n0, n0 + 8) of token t, for tokens in
-// [t_lo, t_hi) and n0 < N. All 128 epilogue threads call this together.
-// GLU: rows 0..63 hold gate and rows 64..127 up values of the 64 features
-// [n_base, n_base + 64); each staged value is rounded to IO (the reference
-// materialises gate_up in IO) and a piece is silu(gate) * up.
-template <typename IO, bool GLU = false, typename Emit>
-__device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* v, int t0, int t_lo, int t_hi,
-                                                    int n_base, int N, Emit&& emit) {
+// Swap orientation: this thread holds v[j] = out(tile row `row`, token
+// t0 + j), j < 32. Stage the 32 x 128 block, rounded to IO, through shared
+// memory as epi[token j][tile row] so it can leave as 16-byte pieces of token
+// rows. All 128 epilogue threads call this together; a readout follows.
+template <typename IO>
+__device__ __forceinline__ void swap_stage(uint16_t* epi, const float* v) {
   const int row = epi_row();
   named_bar_sync(1, kEpiThreads);  // previous chunk fully read
 #pragma unroll
@@ -515,28 +514,52 @@ __device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* 
     epi[j * kTileP + row] = *reinterpret_cast<uint16_t*>(&h);
   }
   named_bar_sync(1, kEpiThreads);
-  const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
-  if constexpr (GLU) {
+}
+
+// Index of this thread among the 128 epilogue threads.
+__device__ __forceinline__ int epi_tid() { return static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads); }
+
+// Readout of a staged chunk: emit(t, n0, piece) receives the 8 consecutive
+// features [n0, n0 + 8) of token t = t0 + j, for tokens in [t_lo, t_hi) and
+// n0 < N (tile row r is feature n_base + r).
+template <typename Emit>
+__device__ __forceinline__ void swap_readout(const uint16_t* epi, int t0, int t_lo, int t_hi, int n_base, int N,
+                                             Emit&& emit) {
+  const int tid = epi_tid();
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const int idx = tid + k * kEpiThreads;  // 256 pieces: 32 tokens x 8 pieces
-      const int j = idx >> 3, piece = idx & 7;
-      const int t = t0 + j, n0 = n_base + piece * 8;
-      const uint16_t* src = epi + j * kTileP + piece * 8;
-      if (t >= t_lo && t < t_hi && n0 < N)
-        emit(t, n0, silu_mul8<IO, true>(*reinterpret_cast<const uint4*>(src),
-                                        *reinterpret_cast<const uint4*>(src + kTileP / 2)));
-    }
-  } else {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int idx = tid + k * kEpiThreads;  // 512 pieces: 32 tokens x 16 pieces
-      const int j = idx >> 4, piece = idx & 15;
-      const int t = t0 + j, n0 = n_base + piece * 8;
-      if (t >= t_lo && t < t_hi && n0 < N)
-        emit(t, n0, *reinterpret_cast<const uint4*>(epi + j * kTileP + piece * 8));
-    }
+  for (int k = 0; k < 4; ++k) {
+    const int idx = tid + k * kEpiThreads;  // 512 pieces: 32 tokens x 16 pieces
+    const int j = idx >> 4, piece = idx & 15;
+    const int t = t0 + j, n0 = n_base + piece * 8;
+    if (t >= t_lo && t < t_hi && n0 < N) emit(t, n0, *reinterpret_cast<const uint4*>(epi + j * kTileP + piece * 8));
   }
+}
+
+// Gated readout: tile rows 0..63 hold gate and rows 64..127 up values of the
+// 64 features [n_base, n_base + 64), already rounded to IO by swap_stage (the
+// reference materialises gate_up in IO); a piece is silu(gate) * up.
+template <typename IO, typename Emit>
+__device__ __forceinline__ void swap_readout_glu(const uint16_t* epi, int t0, int t_lo, int t_hi, int n_base, int N,
+                                                 Emit&& emit) {
+  const int tid = epi_tid();
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int idx = tid + k * kEpiThreads;  // 256 pieces: 32 tokens x 8 pieces
+    const int j = idx >> 3, piece = idx & 7;
+    const int t = t0 + j, n0 = n_base + piece * 8;
+    const uint16_t* src = epi + j * kTileP + piece * 8;
+    if (t >= t_lo && t < t_hi && n0 < N)
+      emit(t, n0, silu_mul8<IO, true>(*reinterpret_cast<const uint4*>(src),
+                                      *reinterpret_cast<const uint4*>(src + kTileP / 2)));
+  }
+}
+
+// swap_stage followed by the plain readout.
+template <typename IO, typename Emit>
+__device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* v, int t0, int t_lo, int t_hi,
+                                                    int n_base, int N, Emit&& emit) {
+  swap_stage<IO>(epi, v);
+  swap_readout(epi, t0, t_lo, t_hi, n_base, N, emit);
 }
 
 // Split tile (swap orientation), called by the 128 epilogue threads of each
@@ -550,15 +573,16 @@ __device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* 
 //      the load/store unit) the others' pieces of its own columns into its
 //      pipeline ring, which is idle after its last MMA;
 //   3. sums its columns in split order (its own values were parked in its
-//      ring in step 1), adds the bias once, rounds and hands 16-byte pieces
-//      of token rows to emit(t, n0, uint4) through the shared staging tile
-//      (GLU: pieces of silu(gate) * up, see swap_epilogue_store);
+//      ring in step 1), adds this thread's row bias `bias_v` once and hands
+//      each 32-token chunk to store_chunk(v, t0, t_lo, t_hi) (all 128
+//      threads together, as the whole-tile epilogue does: v[j] is token
+//      t0 + j, tokens outside [t_lo, t_hi) are not stored);
 //   4. bumps the tile's second counter; the last CTA to finish resets both,
 //      so the counters are zero again for the next launch.
 // Returns false (and records an error) if a wait runs out.
-template <typename IO, int BN, bool GLU = false, typename Emit16>
+template <int BN, typename StoreChunk>
 __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg& sg, const GemmCtl& c, uint32_t tmem,
-                                                  int acc, const IO* bias, Emit16&& emit) {
+                                                  int acc, float bias_v, StoreChunk&& store_chunk) {
   const int S = sg.nctb, j = sg.contrib, u = sg.tile - g.split_first;
   const int row = epi_row();
   const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
@@ -641,8 +665,6 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
   //    memory only and branch-free: token indices past this CTA's run are
   //    clamped (those lanes of the staging tile are not emitted).
   if (ok && n_mine > 0) {
-    const int nf = swap_weight_row<GLU>(g, sg.p, row);
-    const float b = (bias != nullptr && nf >= 0) ? io_to_f32<IO>(bias[nf]) : 0.f;
     const float* base = recv + row;
 #pragma unroll 1
     for (int c0 = 0; c0 < n_mine; c0 += 32) {
@@ -659,10 +681,9 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
         for (int jj = 0; jj < 32; ++jj) v[jj] += sq[static_cast<size_t>(min(jj, lim)) * kTileP];
       }
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) v[jj] += b;
+      for (int jj = 0; jj < 32; ++jj) v[jj] += bias_v;
       if (tid == 0 && c0 == 0) trace(1015);
-      swap_epilogue_store<IO, GLU>(c.epi, v, t_base + my0 + c0, t_base + my0, t_base + my1,
-                                   sg.p * (GLU ? kTileP / 2 : kTileP), g.N, emit);
+      store_chunk(v, t_base + my0 + c0, t_base + my0, t_base + my1);
       if (tid == 0 && c0 == 0) trace(1016);
     }
   }

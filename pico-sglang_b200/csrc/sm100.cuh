@@ -23,6 +23,7 @@ enum DevError : int {
   kDevTimeoutPeer = 2,      // a wait on another rank's flag ran out
   kDevTimeoutGrid = 3,      // a wait on another CTA of this grid ran out
   kDevBadArgs = 4,          // the kernel found inconsistent arguments
+  kDevBadIndex = 5,         // a position or cache-slot index was out of range (token not stored)
 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -98,6 +99,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
 }
 
 // ------------------------------------------------------------------- TMA ---
+// Bring the 128-byte line holding p into L2 (no register result, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -22,6 +22,8 @@ records the same single kernel.
 
 from __future__ import annotations
 
+import functools
+import math
 import threading
 
 import torch
@@ -201,6 +203,129 @@ class GatedMLP(BaseOP):
         else:
             y = self.act_fn(self.gate_up_proj.forward(x))
         return self.down_proj.forward(y)
+
+
+# ----------------------------------------------------------------- rotary --
+
+
+class RotaryEmbedding(BaseOP):
+    """layers/rotary.py:12-32: the [max_position, rotary_dim] float32 table the
+    RoPE kernels read, the cosines of the rotary_dim/2 angles of each position
+    followed by their sines. The angles are position * inv_freq with
+    inv_freq = 1 / base^(2i / rotary_dim), optionally rescaled by
+    `post_process`; the float32 steps are the reference's, so the table is
+    bit-identical to its _cos_sin_cache."""
+
+    def __init__(self, head_size: int, rotary_dim: int, max_position_embeddings: int, base: float,
+                 post_process=None) -> None:
+        if not (0 < rotary_dim <= head_size and rotary_dim % 2 == 0):
+            raise ValueError(f"rotary_dim {rotary_dim} must be even and in (0, {head_size}]")
+        self.head_size = head_size
+        exponents = torch.arange(0, rotary_dim, 2, dtype=torch.float) / rotary_dim
+        inv_freq = 1.0 / (base ** exponents)
+        if post_process is not None:
+            inv_freq = post_process(inv_freq)
+        angles = torch.outer(torch.arange(max_position_embeddings, dtype=torch.float), inv_freq)
+        self._cos_sin_cache = torch.cat((angles.cos(), angles.sin()), dim=-1)
+        self._on_device: dict = {}
+
+    def cache_on(self, device: torch.device) -> torch.Tensor:
+        """The table on `device` (copied once per device)."""
+        if self._cos_sin_cache.device == device:
+            return self._cos_sin_cache
+        c = self._on_device.get(device)
+        if c is None:
+            c = self._on_device[device] = self._cos_sin_cache.to(device).contiguous()
+        return c
+
+
+def _llama3_inv_freq(factor: float, low_freq_factor: float, high_freq_factor: float, original_max: int):
+    """Llama 3 frequency rescaling: wavelengths above original_max / low_freq_factor are slowed
+    by `factor`, those below original_max / high_freq_factor kept, and the band between
+    interpolated linearly in original_max / wavelength (a hard switch if the factors are equal)."""
+
+    def apply(inv_freq: torch.Tensor) -> torch.Tensor:
+        wavelength = 2 * math.pi / inv_freq
+        if low_freq_factor == high_freq_factor:
+            return torch.where(wavelength < original_max / high_freq_factor, inv_freq, inv_freq / factor)
+        t = ((original_max / wavelength - low_freq_factor) / (high_freq_factor - low_freq_factor)).clamp(0, 1)
+        return ((1 - t) / factor + t) * inv_freq
+
+    return apply
+
+
+def _yarn_inv_freq(rotary_dim: int, base: float, factor: float, original_max: int, beta_fast: float,
+                   beta_slow: float):
+    """YaRN frequency blend: dimensions below the beta_fast correction dimension keep their
+    frequency, those above the beta_slow one are divided by `factor`, with a linear ramp between."""
+
+    def correction_dim(rotations: float) -> float:
+        return rotary_dim * math.log(original_max / (rotations * 2 * math.pi)) / (2 * math.log(base))
+
+    lo = max(math.floor(correction_dim(beta_fast)), 0)
+    hi = min(math.ceil(correction_dim(beta_slow)), rotary_dim // 2 - 1)
+
+    def apply(inv_freq: torch.Tensor) -> torch.Tensor:
+        ramp = ((torch.arange(rotary_dim // 2, dtype=torch.float32) - lo) / max(hi - lo, 1)).clamp(0, 1)
+        return (inv_freq / factor) * ramp + inv_freq * (1 - ramp)
+
+    return apply
+
+
+@functools.cache
+def get_rope(head_dim: int, rotary_dim: int, max_position: int, base: float,
+             rope_scaling: tuple | None = None) -> RotaryEmbedding:
+    """layers/rotary.py:63-151: the table for rope_scaling None / default / llama3 / yarn."""
+    cfg = dict(rope_scaling) if rope_scaling is not None else None
+    kind = None if cfg is None else cfg["rope_type"]
+    if kind in (None, "default"):
+        post = None
+    elif kind == "llama3":
+        post = _llama3_inv_freq(cfg["factor"], cfg["low_freq_factor"], cfg["high_freq_factor"],
+                                cfg["original_max_position_embeddings"])
+    elif kind == "yarn":
+        post = _yarn_inv_freq(rotary_dim, base, cfg["factor"], cfg["original_max_position_embeddings"],
+                              cfg.get("beta_fast", 32.0), cfg.get("beta_slow", 1.0))
+    else:
+        raise ValueError(f"Unsupported {rope_scaling = }")
+    return RotaryEmbedding(head_dim, rotary_dim, max_position, base, post)
+
+
+class RotaryAttention(BaseOP):
+    """layers/attention.py:46-117: the same constructor, shards and weight names.
+
+    proj_store(x, positions, out_loc, k_cache, v_cache) is proj
+    (attention.py:94-117) followed by the backend's store_kv
+    (cache/kv/mha_pool.py:45-56) as one kernel: it returns the rotated query
+    [..., nq, hd] and leaves the rotated key and the value in the given layer
+    caches at out_loc. The attention itself belongs to the backend.
+    """
+
+    def __init__(self, hidden_size: int, head_dim: int, num_qo_heads: int, num_kv_heads: int, layer_id: int,
+                 rotary_dim: int, max_position: int, rope_base: float, rope_scaling, *,
+                 has_attn_bias: bool = False, qk_norm_eps: float | None = None):
+        tp = get_tp_info()
+        if qk_norm_eps is not None:
+            raise NotImplementedError("per-head q/k RMSNorm before RoPE is not fused by this library")
+        self.head_dim = head_dim
+        self.num_qo_heads = div_even(num_qo_heads, tp.size)
+        self.num_kv_heads = div_even(num_kv_heads, tp.size, allow_replicate=True)
+        self._layer_id = layer_id
+        self.qkv_proj = LinearColParallelPartitioned(hidden_size, head_dim,
+                                                     [(num_qo_heads, False)] + [(num_kv_heads, True)] * 2,
+                                                     has_bias=has_attn_bias)
+        self.q_norm = None
+        self.k_norm = None
+        self.rotary = get_rope(head_dim, rotary_dim, max_position, rope_base, rope_scaling)
+        self.o_proj = LinearRowParallel(head_dim * num_qo_heads, hidden_size, has_bias=False)
+
+    def proj_store(self, x: torch.Tensor, positions: torch.Tensor, out_loc: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor) -> torch.Tensor:
+        x2 = _flat2d(x).contiguous()
+        q = ops.qkv_rope_store(x2, self.qkv_proj.weight, positions.reshape(-1), out_loc.reshape(-1),
+                               self.rotary.cache_on(x2.device), self.num_qo_heads, self.num_kv_heads,
+                               self.head_dim, k_cache, v_cache, bias=self.qkv_proj.bias)
+        return q.view(*x.shape[:-1], self.num_qo_heads, self.head_dim)
 
 
 class RMSNormFused(BaseOP):

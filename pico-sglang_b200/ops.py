@@ -155,6 +155,104 @@ def silu_and_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tens
     return out
 
 
+_INDEX = {torch.int32: _lib.PGB_I32, torch.int64: _lib.PGB_I64}
+
+
+def _rope_common(positions, out_loc, cos_sin_cache, k_cache, v_cache, T, nkv, hd):
+    for name, t in (("positions", positions), ("out_loc", out_loc), ("cos_sin_cache", cos_sin_cache),
+                    ("k_cache", k_cache), ("v_cache", v_cache)):
+        _require_cuda(name, t)
+    if positions.shape != (T,) or out_loc.shape != (T,):
+        raise ValueError(f"positions and out_loc must be [{T}]")
+    if positions.dtype not in _INDEX or out_loc.dtype != positions.dtype:
+        raise TypeError("positions and out_loc must both be int32 or both int64")
+    if cos_sin_cache.dtype != torch.float32 or cos_sin_cache.dim() != 2:
+        raise TypeError("cos_sin_cache must be a [max_position, rotary_dim] float32 tensor")
+    rows = k_cache.shape[0]
+    for name, c in (("k_cache", k_cache), ("v_cache", v_cache)):
+        if c.numel() != rows * nkv * hd or c.shape[0] != rows:
+            raise ValueError(f"{name} must be [slots, {nkv}, {hd}] (one layer of the KV pool)")
+    return rows
+
+
+def qkv_rope_store(x: torch.Tensor, w: torch.Tensor, positions: torch.Tensor, out_loc: torch.Tensor,
+                   cos_sin_cache: torch.Tensor, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, bias: torch.Tensor | None = None,
+                   q_out: torch.Tensor | None = None) -> torch.Tensor:
+    """qkv_proj + RoPE + KV-cache store in one kernel; returns q [T, nq * hd].
+
+    RotaryAttention.proj (python/picosgl/layers/attention.py:94-117) followed by
+    store_kv (python/picosgl/cache/kv/mha_pool.py:45-56). k_cache / v_cache are
+    one layer's [slots, nkv, hd] storage; out_loc[t] is token t's slot.
+    """
+    _require_cuda("x", x)
+    _require_cuda("weight", w)
+    nq, nkv, hd = num_q_heads, num_kv_heads, head_dim
+    N = (nq + 2 * nkv) * hd
+    if x.dim() != 2 or w.shape != (N, x.shape[1]):
+        raise ValueError(f"shape mismatch: x {tuple(x.shape)} weight {tuple(w.shape)} (expected [{N}, K])")
+    if x.dtype != w.dtype or k_cache.dtype != x.dtype or v_cache.dtype != x.dtype:
+        raise TypeError("x, weight and the caches must share one dtype")
+    T, K = x.shape
+    rows = _rope_common(positions, out_loc, cos_sin_cache, k_cache, v_cache, T, nkv, hd)
+    if bias is not None:
+        _require_cuda("bias", bias)
+        if bias.shape != (N,) or bias.dtype != x.dtype:
+            raise ValueError("bias must be [N] with the input dtype")
+    if q_out is None:
+        q_out = torch.empty((T, nq * hd), dtype=x.dtype, device=x.device)
+    else:
+        _require_cuda("q_out", q_out)
+        if q_out.numel() != T * nq * hd or q_out.dtype != x.dtype:
+            raise ValueError("q_out must hold [T, nq * hd] of the input dtype")
+    lib = _lib.load()
+    need = lib.pgb_qkv_rope_store_workspace_size(T, nq, nkv, hd, K, dtype_code(x))
+    ws = WORKSPACES.get(x.device, need)
+    _lib.call("pgb_qkv_rope_store", x.data_ptr(), w.data_ptr(), bias.data_ptr() if bias is not None else None,
+              T, K, nq, nkv, hd, cos_sin_cache.shape[1], positions.data_ptr(), out_loc.data_ptr(),
+              _INDEX[positions.dtype], cos_sin_cache.data_ptr(), cos_sin_cache.shape[0], q_out.data_ptr(),
+              k_cache.data_ptr(), v_cache.data_ptr(), rows, dtype_code(x), ws.data_ptr(), ws.numel(), _stream(x))
+    return q_out
+
+
+def rope_store(qkv: torch.Tensor, positions: torch.Tensor, out_loc: torch.Tensor, cos_sin_cache: torch.Tensor,
+               num_q_heads: int, num_kv_heads: int, head_dim: int, k_cache: torch.Tensor,
+               v_cache: torch.Tensor, q_out: torch.Tensor | None = None,
+               status: torch.Tensor | None = None) -> torch.Tensor:
+    """RoPE + KV-cache store from a materialised qkv [T, (nq + 2 nkv) hd]
+    (flashinfer apply_rope_with_cos_sin_cache_inplace + store_cache); returns q."""
+    _require_cuda("qkv", qkv)
+    nq, nkv, hd = num_q_heads, num_kv_heads, head_dim
+    T = qkv.shape[0]
+    if qkv.dim() != 2 or qkv.shape[1] != (nq + 2 * nkv) * hd:
+        raise ValueError(f"qkv must be [T, {(nq + 2 * nkv) * hd}]")
+    rows = _rope_common(positions, out_loc, cos_sin_cache, k_cache, v_cache, T, nkv, hd)
+    if q_out is None:
+        q_out = torch.empty((T, nq * hd), dtype=qkv.dtype, device=qkv.device)
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=qkv.device)
+    _lib.call("pgb_rope_store", qkv.data_ptr(), T, nq, nkv, hd, cos_sin_cache.shape[1], positions.data_ptr(),
+              out_loc.data_ptr(), _INDEX[positions.dtype], cos_sin_cache.data_ptr(), cos_sin_cache.shape[0],
+              q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), rows, dtype_code(qkv), status.data_ptr(),
+              _stream(qkv))
+    return q_out
+
+
+def rope_index_error(device: torch.device, reset: bool = False) -> int:
+    """Index-error word of the column-GEMM workspace on `device`: 5 once a
+    qkv_rope_store call skipped a token whose position or cache slot was out
+    of range, else 0. Synchronises."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = WORKSPACES._bufs.get(idx)
+    if buf is None:
+        return 0
+    word = buf[4:8].view(torch.int32)
+    val = int(word.item())
+    if reset:
+        word.zero_()
+    return val
+
+
 def row_gemm_allreduce_addnorm(comm, x_local: torch.Tensor, w_local: torch.Tensor,
                                residual: torch.Tensor | None, norm_w: torch.Tensor | None,
                                eps: float, out: torch.Tensor | None = None,

@@ -29,6 +29,11 @@ What it records:
              (include/flashinfer/activation.cuh, silu from
              flashinfer/jit/activation.py), checked against
              torch.nn.functional.silu before it is used.
+  rope_small.npz  the reference's RoPE cos/sin tables (get_rope,
+             python/picosgl/layers/rotary.py:63-151) for default, partial
+             (rotary_dim < head_dim), llama3 and yarn scaling. Applying them
+             needs FlashInfer on a GPU (rotary.py:48-59), so only the tables
+             are recorded here.
 """
 
 from __future__ import annotations
@@ -262,9 +267,32 @@ def make_mlp_small():
     np.savez_compressed(HERE / "mlp_small.npz", **data)
 
 
+ROPE_CASES = {
+    "default_hd128": (128, 128, 96, 1e6, None),
+    "partial_hd128_rd64": (128, 64, 96, 1e4, None),
+    "default_hd64": (64, 64, 96, 1e4, None),
+    "llama3": (128, 128, 96, 5e5, (("rope_type", "llama3"), ("factor", 8.0), ("low_freq_factor", 1.0),
+                                   ("high_freq_factor", 4.0), ("original_max_position_embeddings", 64))),
+    "yarn": (128, 128, 96, 1e6, (("rope_type", "yarn"), ("factor", 4.0),
+                                 ("original_max_position_embeddings", 64))),
+}
+
+
+def make_rope_small():
+    _ref_imports()
+    from picosgl.layers.rotary import get_rope
+
+    data = {}
+    for name, (hd, rd, max_pos, base, scaling) in ROPE_CASES.items():
+        data[name] = get_rope(hd, rd, max_pos, base, scaling)._cos_sin_cache.numpy().copy()
+    data["meta"] = np.array(repr(ROPE_CASES))
+    np.savez_compressed(HERE / "rope_small.npz", **data)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
     make_tp_small()
     make_mlp_small()
+    make_rope_small()
     make_cfg1()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))

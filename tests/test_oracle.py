@@ -199,3 +199,69 @@ def test_gate_up_silu_ragged_and_empty():
     ref = gu[:, :5] / (1 + np.exp(-gu[:, :5])) * gu[:, 5:]
     assert np.allclose(y, ref, rtol=1e-5, atol=1e-6)
     assert oracle.gate_up_silu(x[:0], w, dtype="bf16").shape == (0, 5)
+
+
+@pytest.fixture(scope="module")
+def rope_small():
+    return dict(np.load(GOLD / "rope_small.npz"))
+
+
+ROPE_CASES = {
+    "default_hd128": (128, 128, 96, 1e6, None),
+    "partial_hd128_rd64": (128, 64, 96, 1e4, None),
+    "default_hd64": (64, 64, 96, 1e4, None),
+    "llama3": (128, 128, 96, 5e5, (("rope_type", "llama3"), ("factor", 8.0), ("low_freq_factor", 1.0),
+                                   ("high_freq_factor", 4.0), ("original_max_position_embeddings", 64))),
+    "yarn": (128, 128, 96, 1e6, (("rope_type", "yarn"), ("factor", 4.0),
+                                 ("original_max_position_embeddings", 64))),
+}
+
+
+@pytest.mark.parametrize("name", sorted(ROPE_CASES))
+def test_rope_table_matches_reference(rope_small, name):
+    """The layer mirror's cos/sin table (what the kernels read) is bit-identical
+    to the reference's get_rope table (python/picosgl/layers/rotary.py:63-151)."""
+    import importlib
+
+    L = importlib.import_module("pico-sglang_b200.layers")
+    hd, rd, mp, base, sc = ROPE_CASES[name]
+    assert np.array_equal(L.get_rope(hd, rd, mp, base, sc)._cos_sin_cache.numpy(), rope_small[name])
+
+
+def test_rope_oracle_properties(rope_small):
+    """NeoX RoPE: position 0 is the identity; each (i, i + rd/2) pair keeps its
+    norm; dims from rd on are untouched; rotating by p then reading the pair
+    as a complex number equals multiplying by exp(i * angle) (f32 tolerance)."""
+    table = rope_small["partial_hd128_rd64"]
+    hd, rd = 128, 64
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((5, 2 * hd)).astype(np.float32)
+    pos = np.array([0, 1, 7, 50, 95])
+    y = oracle.apply_rope_neox(x, pos, table, hd, "f32")
+    assert np.array_equal(y[0], x[0])
+    xh, yh = x.reshape(5, 2, hd), y.reshape(5, 2, hd)
+    assert np.array_equal(yh[..., rd:], xh[..., rd:])
+    n_in = xh[..., : rd // 2] ** 2 + xh[..., rd // 2: rd] ** 2
+    n_out = yh[..., : rd // 2] ** 2 + yh[..., rd // 2: rd] ** 2
+    assert np.allclose(n_in, n_out, rtol=1e-5, atol=1e-6)
+    z = (xh[..., : rd // 2] + 1j * xh[..., rd // 2: rd]).astype(np.complex128)
+    ang = np.arctan2(table[pos, rd // 2:], table[pos, : rd // 2])[:, None, :]
+    zr = z * np.exp(1j * ang)
+    assert np.allclose(yh[..., : rd // 2], zr.real, atol=2e-5) and np.allclose(yh[..., rd // 2: rd], zr.imag, atol=2e-5)
+
+
+def test_qkv_rope_store_oracle_scatters_rows():
+    rng = np.random.default_rng(4)
+    T, K, nq, nkv, hd = 3, 32, 2, 1, 64
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    w = (rng.standard_normal(((nq + 2 * nkv) * hd, K)) * 0.1).astype(np.float32)
+    table = np.concatenate([np.ones((8, 32)), np.zeros((8, 32))], 1).astype(np.float32)  # identity rotation
+    kc = np.full((10, nkv, hd), 7.0, np.float32)
+    vc = np.full((10, nkv, hd), 7.0, np.float32)
+    q, kc2, vc2 = oracle.qkv_rope_store(x, w, None, [1, 2, 3], [9, 0, 4], table, nq, nkv, hd, kc, vc, "f32")
+    qkv = oracle.linear(x, w, dtype="f32")
+    assert np.array_equal(q, qkv[:, : nq * hd])
+    assert np.array_equal(kc2[[9, 0, 4]].reshape(T, -1), qkv[:, nq * hd: (nq + nkv) * hd])
+    assert np.array_equal(vc2[[9, 0, 4]].reshape(T, -1), qkv[:, (nq + nkv) * hd:])
+    untouched = [i for i in range(10) if i not in (9, 0, 4)]
+    assert np.all(kc2[untouched] == 7.0) and np.all(vc2[untouched] == 7.0)
