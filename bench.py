@@ -18,7 +18,9 @@ outputs are fixed synthetic activations. The gated MLP's front half
 (gate_up_proj + silu_and_mul, fused by pgb_gate_up_silu) is timed beside the
 step under `config.mlp_front_us`, and the attention block's front (qkv_proj +
 RoPE + KV-cache store, fused by pgb_qkv_rope_store) under
-`config.attn_front_us`. L is chosen so the step's weights
+`config.attn_front_us`. On one GPU, `config.full_layer_us` times the whole decoder layer
+minus the attention itself (all four fused kernels through the public API) against the
+reference's own unfused calls on the same weights. L is chosen so the step's weights
 exceed 3x the 126 MB L2, so every layer streams its weights from HBM (no L2
 flush is needed). The step is captured once in a CUDA graph (as the
 reference's decode graphs, engine/graph.py:100-142) and replayed.
@@ -346,8 +348,9 @@ def run_ours(args) -> dict | None:
         breakdown[name] = round(ms_op * 1000.0 / args.steps / n_layers, 3)
         del gg
     breakdown["gate_up"] = round(gu_us, 3)
-    mlp_front = mlp_front_timings(args, pgb, layers, x1, stream, barrier, n_layers)
-    attn_front = attn_front_timings(args, pgb, L, layers, st.h, stream, barrier, n_layers, n, dev)
+    mlp_front = mlp_front_timings(args, pgb, layers, x1, stream, barrier, n_layers) if args.extras else None
+    attn_front = (attn_front_timings(args, pgb, L, layers, st.h, stream, barrier, n_layers, n, dev)
+                  if args.extras else None)
 
     # End to end through the public API: pinned host inputs copied in, the
     # captured layer stack replayed, the output and residual copied out.
@@ -388,12 +391,21 @@ def run_ours(args) -> dict | None:
     e2e_us = ms_e.item() * 1000.0 / args.steps / n_layers
 
     lib = library_path_baseline(args, n, rank, world, dev, stream, barrier, T) if args.library_baseline else None
+    lib_small = None
+    if args.library_baseline and 1 in args.tokens and T != 1:
+        lib_small = library_path_baseline(args, n, rank, world, dev, stream, barrier, 1)
+    full = None
+    if world == 1 and args.extras:
+        full = {str(t): full_layer_timings(args, pgb, L, layers, dev, stream, barrier, n_layers, t)
+                for t in sorted({1, T} & set(args.tokens) | {T})}
 
     result = None
     if rank == 0:
         head = per_t[T]
         cpu = cpu_baseline(T) if (world == 1 and not args.no_cpu_baseline) else None
-        launches = 4 * n_layers * args.steps
+        # One rank: o_proj and down_proj each run as the column GEMM + the norm
+        # kernel (pgb_comm_set_one_rank_path); more ranks: one fused kernel each.
+        launches = (4 if world > 1 else 6) * n_layers * args.steps
         result = {
             "metric": "fused TP GEMM+allreduce+RMSNorm us/layer (decode, config 2)",
             "value": head["us_per_layer"],
@@ -447,6 +459,10 @@ def run_ours(args) -> dict | None:
             result["cpu_baseline"] = cpu
         if lib:
             result["library_baseline"] = lib
+        if lib_small:
+            result["library_baseline_T1"] = lib_small
+        if full:
+            result["config"]["full_layer_us"] = full
     if world > 1:
         D.destroy_distributed()
         dist.destroy_process_group()
@@ -548,6 +564,74 @@ def attn_front_timings(args, pgb, L, layers, h, stream, barrier, n_layers, n, de
         if dist_is_initialized():
             torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
         out[name] = round(ms_t.item() * 1000.0 / args.steps / n_layers, 3)
+        del gg
+    return out
+
+
+def full_layer_timings(args, pgb, L, layers, dev, stream, barrier, n_layers, T) -> dict:
+    """A decoder layer without the attention itself, one GPU, per layer, two ways on the same
+    weights. This library's public API: qkv_rope_store (qkv_proj + RoPE + KV store), o_proj
+    linked to post_attention_layernorm (GEMM + residual add + RMSNorm in one kernel),
+    gate_up_silu, down_proj linked to the next input_layernorm. The reference's own calls
+    (python/picosgl/layers/attention.py:94-123, mlp.py:43-48, norm.py:73-75): F.linear, the
+    FlashInfer RoPE on the strided split, an index store into the cache, F.linear +
+    fused_add_rmsnorm, F.linear + silu_and_mul, F.linear + fused_add_rmsnorm. The attention
+    output is a fixed synthetic [T, H] tensor in both."""
+    import torch.nn.functional as F
+
+    g = torch.Generator(device=dev).manual_seed(21 + T)
+    h = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    a = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    res = torch.randn(T, H, device=dev, generator=g).bfloat16()
+    table = L.get_rope(HD, HD, 4096, 1e6, None).cache_on(dev)
+    pos = torch.randint(0, 4096, (T,), generator=g, device=dev, dtype=torch.int32)
+    loc = torch.randperm(4096, generator=g, device=dev)[:T].to(torch.int32)
+    loc64 = loc.long()
+    caches = [(torch.zeros(4096, NKV, HD, device=dev, dtype=torch.bfloat16),
+               torch.zeros(4096, NKV, HD, device=dev, dtype=torch.bfloat16)) for _ in layers]
+
+    def ours():
+        L.reset_fusion_context()
+        L._CTX.residual = res
+        x = h
+        for lay, (kc, vc) in zip(layers, caches):
+            pgb.ops.qkv_rope_store(x, lay["qkv"].weight, pos, loc, table, NQ, NKV, HD, kc, vc)
+            x1 = lay["o"].forward(a)
+            x1, _ = lay["ln1"].forward(x1, res)
+            m = pgb.gate_up_silu(x1, lay["gate_up"].weight)
+            x2 = lay["down"].forward(m)
+            x, _ = lay["ln2"].forward(x2, res)
+
+    ways = {"ours": ours}
+    try:
+        import flashinfer
+
+        ln = torch.ones(H, device=dev).bfloat16()
+
+        def library():
+            x = h
+            for lay, (kc, vc) in zip(layers, caches):
+                qkv = F.linear(x, lay["qkv"].weight)
+                q, k, v = qkv.split([NQ * HD, NKV * HD, NKV * HD], dim=-1)
+                flashinfer.apply_rope_with_cos_sin_cache_inplace(pos, q, k, HD, table, is_neox=True)
+                kc[loc64] = k.view(T, NKV, HD)
+                vc[loc64] = v.view(T, NKV, HD)
+                y = F.linear(a, lay["o"].weight)
+                flashinfer.fused_add_rmsnorm(y, res, ln, EPS)
+                m = flashinfer.silu_and_mul(F.linear(y, lay["gate_up"].weight))
+                x = F.linear(m, lay["down"].weight)
+                flashinfer.fused_add_rmsnorm(x, res, ln, EPS)
+
+        if args.library_baseline:
+            ways["library"] = library
+    except Exception:  # pragma: no cover - flashinfer missing
+        pass
+    out = {"tokens": int(T)}
+    for name, fn in ways.items():
+        with torch.cuda.stream(stream):
+            gg = capture(fn, stream)
+            ms = time_graph(gg, stream, args.steps, args.warmup, barrier)
+        out[name] = round(ms * 1000.0 / args.steps / n_layers, 3)
         del gg
     return out
 
@@ -723,6 +807,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-library-baseline", dest="library_baseline", action="store_false")
+    ap.add_argument("--no-extras", dest="extras", action="store_false",
+                    help="skip the side measurements (MLP / attention fronts, full layer); the step is unchanged")
     args = ap.parse_args()
     args.tokens = [int(t) for t in args.tokens.split(",")]
     if args.warmup < 3:

@@ -106,6 +106,14 @@ PGB_API int pgb_comm_destroy(pgb_comm* comm);
 /* Budget of every device-side wait on a peer (default 30 s). */
 PGB_API int pgb_comm_set_timeout_ns(pgb_comm* comm, uint64_t ns);
 
+/* One-rank communicators only: 1 runs pgb_row_gemm_allreduce_addnorm as the
+ * fused cooperative kernel; 0 (the default) runs the column GEMM followed by
+ * pgb_fused_add_rmsnorm, two launches that are faster when there is no
+ * all-reduce to overlap (the reference's own sequence at TP = 1,
+ * python/picosgl/layers/linear.py:90-97 then norm.py:73-75). Results are the
+ * same. No reference counterpart. */
+PGB_API int pgb_comm_set_one_rank_path(pgb_comm* comm, int fused);
+
 /* Read the device status word (0 = ok, else PGB_ERR_TIMEOUT etc. as the
  * device recorded it); reset it to 0 when reset != 0. Synchronises the
  * device. */
@@ -235,6 +243,8 @@ PGB_API int pgb_rope_store(const void* qkv, int T, int num_q_heads, int num_kv_h
  * with a residual (python/picosgl/layers/norm.py:56-75). With norm_w == NULL
  * the kernel stops after the reduction and writes y to out (residual unused),
  * which is LinearRowParallel.forward alone. out may alias nothing else.
+ * On a one-rank communicator this is the column GEMM into out followed by
+ * pgb_fused_add_rmsnorm (see pgb_comm_set_one_rank_path).
  * Returns PGB_ERR_INVALID for shapes the communicator's buffer cannot hold. */
 PGB_API int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_local, const void* w_local,
                                    const void* bias, void* residual, const void* norm_w,

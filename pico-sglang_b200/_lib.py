@@ -63,6 +63,7 @@ _SIGS: dict[str, tuple[object, list[object]]] = {
     "pgb_comm_destroy": (c_int, [c_void_p]),
     "pgb_comm_set_timeout_ns": (c_int, [c_void_p, c_uint64]),
     "pgb_comm_get_status": (c_int, [c_void_p, POINTER(c_int), c_int]),
+    "pgb_comm_set_one_rank_path": (c_int, [c_void_p, c_int]),
     "pgb_comm_get_buffer": (c_int, [c_void_p, POINTER(c_void_p)]),
     "pgb_all_reduce": (c_int, [c_void_p, c_void_p, c_size_t, c_int, c_int, c_void_p]),
     "pgb_all_gather": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_int, c_void_p]),

@@ -244,11 +244,11 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
 }
 
 // Launch one column kernel. N is the output width g.N; the weight has N rows,
-// or 2N ([gate; up]) for a gated policy. ws is the column workspace
-// ([status | counters | exchange], col_workspace_bytes).
+// or 2N ([gate; up]) for a gated policy. sc is the split-K scratch (a column
+// workspace, col_scratch(), or a communicator's device-local area).
 template <typename IO, int BN, bool SWAP, typename Epi>
 int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
-               uint8_t* ws, size_t ws_bytes, cudaStream_t stream, const Epi& epi) {
+               const ColScratch& sc, cudaStream_t stream, const Epi& epi) {
   constexpr int STAGES = gemm_stages<BN>();
   using L = GemmSmem<BN, STAGES, Epi::kSmemBytes>;
   static_assert(L::kBytes <= 232448, "shared memory budget");
@@ -260,10 +260,10 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
   PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
   if (p.nsplit > 1 && split_recv_bytes(BN, p.nsplit) > static_cast<size_t>(STAGES) * L::kStageBytes)
     return set_error(PGB_ERR_STATE, "col_gemm: split of %d does not fit the pipeline ring", p.nsplit);
-  if (col_workspace_bytes(p) > ws_bytes)
-    return set_error(PGB_ERR_INVALID, "col_gemm: workspace of %zu bytes, %zu needed", ws_bytes,
-                     col_workspace_bytes(p));
-  if (p.counter_bytes > kWsCounterBytes)
+  if (p.exchange_bytes > sc.xchg_bytes)
+    return set_error(PGB_ERR_INVALID, "col_gemm: split exchange of %zu bytes, scratch holds %zu", p.exchange_bytes,
+                     sc.xchg_bytes);
+  if (p.counter_bytes > sc.ctr_bytes)
     return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d split tiles exceed the counter region",
                      p.tiles - p.split_first);
 
@@ -289,9 +289,9 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
   g.grid = p.grid;
   g.split_ctas = p.split_ctas;
   g.nsplit = p.nsplit;
-  g.status = reinterpret_cast<int*>(ws);
-  g.ctr = reinterpret_cast<uint32_t*>(ws + kWsHeaderBytes);
-  g.xchg = reinterpret_cast<float*>(ws + kWsHeaderBytes + kWsCounterBytes);
+  g.status = sc.status;
+  g.ctr = sc.ctr;
+  g.xchg = sc.xchg;
   g.wait_ns = 2000000000ull;  // 2 s: far beyond any legitimate pipeline stall
   g.glu = Epi::kGlu ? 1 : 0;
 
@@ -309,13 +309,13 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
 // The tile width the plan picked, for one policy.
 template <typename IO, typename Epi>
 int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
-                 uint8_t* ws, size_t wsb, cudaStream_t stream, const Epi& epi) {
-  if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
+                 const ColScratch& sc, cudaStream_t stream, const Epi& epi) {
+  if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, T, N, K, sc, stream, epi);
   switch (p.bn) {
-    case 32: return launch_col<IO, 32, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
-    case 64: return launch_col<IO, 64, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
-    case 128: return launch_col<IO, 128, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
-    case 256: return launch_col<IO, 256, true>(p, dev, x, w, T, N, K, ws, wsb, stream, epi);
+    case 32: return launch_col<IO, 32, true>(p, dev, x, w, T, N, K, sc, stream, epi);
+    case 64: return launch_col<IO, 64, true>(p, dev, x, w, T, N, K, sc, stream, epi);
+    case 128: return launch_col<IO, 128, true>(p, dev, x, w, T, N, K, sc, stream, epi);
+    case 256: return launch_col<IO, 256, true>(p, dev, x, w, T, N, K, sc, stream, epi);
     default: return set_error(PGB_ERR_INVALID, "no kernel for tile width %d", p.bn);
   }
 }

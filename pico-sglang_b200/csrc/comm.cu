@@ -396,6 +396,12 @@ extern "C" int pgb_comm_set_timeout_ns(pgb_comm* comm, uint64_t ns) {
   return PGB_OK;
 }
 
+extern "C" int pgb_comm_set_one_rank_path(pgb_comm* comm, int fused) {
+  if (comm == nullptr) return set_error(PGB_ERR_INVALID, "set_one_rank_path: null communicator");
+  comm->one_rank_fused = fused != 0 ? 1 : 0;
+  return PGB_OK;
+}
+
 extern "C" int pgb_comm_get_status(pgb_comm* comm, int* out, int reset) {
   if (comm == nullptr || out == nullptr) return set_error(PGB_ERR_INVALID, "get_status: null argument");
   DeviceGuard g(comm->device);

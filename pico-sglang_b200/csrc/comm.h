@@ -90,6 +90,7 @@ struct pgb_comm {
   uint64_t result_parity_bytes;
   uint64_t timeout_ns;
   int sm_count;
+  int one_rank_fused = 0;  // world == 1: run the row op as the fused kernel (else GEMM + norm)
 };
 
 namespace pgb {

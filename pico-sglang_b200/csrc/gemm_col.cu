@@ -26,6 +26,23 @@ int sm_count_or_default() {
 
 }  // namespace
 
+int col_gemm_on_scratch(const void* x, const void* w, const void* bias, void* y, int T, int N, int K, int dtype,
+                        const ColScratch& sc, void* stream) {
+  DeviceInfo dev;
+  int rc = current_device_info(&dev);
+  if (rc) return rc;
+  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, sc.xchg_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == PGB_BF16)
+    return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, N, K, sc, s,
+                                       EpiPlain<__nv_bfloat16>{static_cast<__nv_bfloat16*>(y),
+                                                               static_cast<const __nv_bfloat16*>(bias)});
+  if (dtype == PGB_F16)
+    return dispatch_col<__half>(p, dev, x, w, T, N, K, sc, s,
+                                EpiPlain<__half>{static_cast<__half*>(y), static_cast<const __half*>(bias)});
+  return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: dtype %d not supported", dtype);
+}
+
 }  // namespace pgb
 
 extern "C" size_t pgb_col_gemm_workspace_size(int T, int N, int K) {
@@ -67,11 +84,12 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
                      need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const ColScratch sc = col_scratch(ws, workspace_bytes);
   if (dtype == PGB_BF16)
-    return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, N, K, ws, workspace_bytes, s,
+    return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, N, K, sc, s,
                                        EpiPlain<__nv_bfloat16>{static_cast<__nv_bfloat16*>(y),
                                                                static_cast<const __nv_bfloat16*>(bias)});
-  return dispatch_col<__half>(p, dev, x, w, T, N, K, ws, workspace_bytes, s,
+  return dispatch_col<__half>(p, dev, x, w, T, N, K, sc, s,
                               EpiPlain<__half>{static_cast<__half*>(y), static_cast<const __half*>(bias)});
 }
 
@@ -135,11 +153,12 @@ extern "C" int pgb_gate_up_silu(const void* x, const void* w, const void* bias, 
     return set_error(PGB_ERR_INVALID, "gate_up_silu: workspace of %zu bytes, %zu needed", workspace_bytes,
                      need);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
+  const ColScratch sc = col_scratch(ws, workspace_bytes);
   if (dtype == PGB_BF16)
-    return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, I, K, ws, workspace_bytes, s,
+    return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, I, K, sc, s,
                                        EpiGlu<__nv_bfloat16>{static_cast<__nv_bfloat16*>(out),
                                                              static_cast<const __nv_bfloat16*>(bias)});
-  return dispatch_col<__half>(p, dev, x, w, T, I, K, ws, workspace_bytes, s,
+  return dispatch_col<__half>(p, dev, x, w, T, I, K, sc, s,
                               EpiGlu<__half>{static_cast<__half*>(out), static_cast<const __half*>(bias)});
 }
 

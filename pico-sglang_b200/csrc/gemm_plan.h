@@ -43,4 +43,31 @@ inline size_t col_workspace_bytes(const GemmPlan& p) {
   return kWsHeaderBytes + kWsCounterBytes + p.exchange_bytes;
 }
 
+// Split-K scratch of one column GEMM launch: status word, per-split-tile
+// counters (zero at rest) and the f32 exchange area.
+struct ColScratch {
+  int* status;
+  uint32_t* ctr;
+  size_t ctr_bytes;
+  float* xchg;
+  size_t xchg_bytes;
+};
+
+// The scratch inside a column workspace of ws_bytes (>= kWsHeaderBytes + kWsCounterBytes).
+inline ColScratch col_scratch(uint8_t* ws, size_t ws_bytes) {
+  ColScratch sc;
+  sc.status = reinterpret_cast<int*>(ws);
+  sc.ctr = reinterpret_cast<uint32_t*>(ws + kWsHeaderBytes);
+  sc.ctr_bytes = kWsCounterBytes;
+  sc.xchg = reinterpret_cast<float*>(ws + kWsHeaderBytes + kWsCounterBytes);
+  sc.xchg_bytes = ws_bytes > kWsHeaderBytes + kWsCounterBytes ? ws_bytes - kWsHeaderBytes - kWsCounterBytes : 0;
+  return sc;
+}
+
+// Plain column GEMM y = x . w^T (+ bias), 16-bit dtype, on caller-provided
+// scratch, planned for `sms` SMs with the exchange capped at the scratch's
+// size (gemm_col.cu). Used by the one-rank row-parallel path.
+int col_gemm_on_scratch(const void* x, const void* w, const void* bias, void* y, int T, int N, int K, int dtype,
+                        const ColScratch& sc, void* stream);
+
 }  // namespace pgb

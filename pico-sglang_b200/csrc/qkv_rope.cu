@@ -428,13 +428,13 @@ extern "C" int pgb_qkv_rope_store(const void* x, const void* w, const void* bias
                                     max_position, idx64, nq, nkv, hd, rd,
                                     reinterpret_cast<int*>(ws + kWsIndexErrorOffset)),
                          static_cast<const B*>(bias)};
-    return dispatch_col<B>(p, dev, x, w, T, N, K, ws, workspace_bytes, s, epi);
+    return dispatch_col<B>(p, dev, x, w, T, N, K, col_scratch(ws, workspace_bytes), s, epi);
   }
   const EpiRope<__half> epi{make_rs<__half>(q_out, k_cache, v_cache, positions, out_loc, cos_sin_cache, cache_rows,
                                             max_position, idx64, nq, nkv, hd, rd,
                                             reinterpret_cast<int*>(ws + kWsIndexErrorOffset)),
                             static_cast<const __half*>(bias)};
-  return dispatch_col<__half>(p, dev, x, w, T, N, K, ws, workspace_bytes, s, epi);
+  return dispatch_col<__half>(p, dev, x, w, T, N, K, col_scratch(ws, workspace_bytes), s, epi);
 }
 
 extern "C" int pgb_rope_store(const void* qkv, int T, int num_q_heads, int num_kv_heads, int head_dim,

@@ -140,6 +140,11 @@ class PGBCommunicator:
         _lib.call("pgb_comm_get_buffer", self._h, ctypes.byref(out))
         return out
 
+    def set_one_rank_path(self, fused: bool) -> None:
+        """One rank only: run the row op as the fused kernel (True) or as the
+        column GEMM followed by fused_add_rmsnorm (False, the default)."""
+        _lib.call("pgb_comm_set_one_rank_path", self._h, int(bool(fused)))
+
     # -- health -------------------------------------------------------------
     def set_timeout(self, seconds: float) -> None:
         _lib.call("pgb_comm_set_timeout_ns", self._h, int(seconds * 1e9))

@@ -56,12 +56,15 @@ def within(a, ref, tol=2e-2, ulps=2):
     return worst <= 1.0, f"max|diff|={d.max().item():.4g} rms={rms:.4g} worst/bound={worst:.3g}"
 
 
-@pytest.fixture(scope="module")
-def comm1(pgb):
+@pytest.fixture(scope="module", params=["gemm_then_norm", "fused_kernel"])
+def comm1(pgb, request):
+    """A one-rank communicator, on each of its two row paths: the column GEMM
+    followed by fused_add_rmsnorm (the default) and the fused kernel."""
     import importlib
 
     dist = importlib.import_module("pico-sglang_b200.distributed")
     c = dist.PGBCommunicator(0, 1, 64 << 20, dist.create_uid())
+    c.set_one_rank_path(request.param == "fused_kernel")
     yield c
     c.close()
 
