@@ -101,3 +101,59 @@ def test_work_decomposition_covers_every_k_block_once(pgb, sms):
                 if lib.pgb_check_work_plan(T, N, K, sms, all_sk, grid, clusters) != 0:
                     bad.append((T, N, K, all_sk, clusters, lib.pgb_last_error().decode()))
     assert not bad, bad[:5]
+
+
+def test_fused_epilogue_entry_points_reject_bad_arguments_before_the_device(pgb):
+    """gate_up + silu, qkv + RoPE + store and the standalone kernels check their
+    arguments on the host and return a status; nothing here needs a GPU."""
+    lib = pgb._lib.load()
+    L = pgb._lib
+    ws = ctypes.c_size_t(1 << 20)
+    # gate_up_silu: I not a multiple of 8, an unknown dtype, T == 0 (nothing to do)
+    rc = lib.pgb_gate_up_silu(1, 1, None, 1, 4, 12, 256, L.PGB_BF16, 1, ws, None)
+    assert rc == L.PGB_ERR_INVALID and "multiples of 8" in _last_error(lib)
+    assert lib.pgb_gate_up_silu(1, 1, None, 1, 4, 16, 256, 9, 1, ws, None) == L.PGB_ERR_UNSUPPORTED
+    assert lib.pgb_gate_up_silu(1, 1, None, 1, 0, 16, 256, L.PGB_BF16, 1, ws, None) == L.PGB_OK
+    assert lib.pgb_gate_up_silu(None, 1, None, 1, 4, 16, 256, L.PGB_BF16, 1, ws, None) == L.PGB_ERR_INVALID
+    # silu_and_mul: bad width, null pointers, empty input
+    assert lib.pgb_silu_and_mul(1, 1, 4, 0, L.PGB_BF16, None) == L.PGB_ERR_INVALID
+    assert lib.pgb_silu_and_mul(None, 1, 4, 8, L.PGB_BF16, None) == L.PGB_ERR_INVALID
+    assert lib.pgb_silu_and_mul(1, 1, 0, 8, L.PGB_BF16, None) == L.PGB_OK
+
+    def qkv(hd=128, rd=128, idx=L.PGB_I32, T=4, rows=64):
+        return lib.pgb_qkv_rope_store(16, 16, None, T, 256, 4, 1, hd, rd, 16, 16, idx, 16, 64, 16, 16, 16, rows,
+                                      L.PGB_BF16, 16, ws, None)
+
+    assert qkv(hd=96) == L.PGB_ERR_UNSUPPORTED and "head_dim" in _last_error(lib)
+    assert qkv(rd=32) == L.PGB_ERR_UNSUPPORTED and "rotary_dim" in _last_error(lib)
+    assert qkv(rd=192) == L.PGB_ERR_UNSUPPORTED
+    assert qkv(idx=7) == L.PGB_ERR_INVALID and "index dtype" in _last_error(lib)
+    assert qkv(rows=1 << 40) == L.PGB_ERR_INVALID  # slots beyond int32
+    assert qkv(T=0) == L.PGB_OK
+    rc = lib.pgb_qkv_rope_store(16, 16, None, 4, 256, 4, 1, 128, 128, 16, 16, L.PGB_I32, 16, 64, 24, 16, 16, 64,
+                                L.PGB_BF16, 16, ws, None)
+    assert rc == L.PGB_ERR_INVALID and "16-byte aligned" in _last_error(lib)
+    rc = lib.pgb_rope_store(16, 4, 4, 1, 128, 128, 16, 16, L.PGB_I32, 16, 64, 16, 16, 16, 64, L.PGB_BF16, None, None)
+    assert rc == L.PGB_ERR_INVALID and "null" in _last_error(lib)
+    # workspace sizes: the gated op plans the [T, 2I] GEMM; f32 adds its intermediate
+    assert lib.pgb_gate_up_silu_workspace_size(8, 12288, 4096, L.PGB_BF16) == \
+        lib.pgb_col_gemm_workspace_size(8, 24576, 4096)
+    assert lib.pgb_qkv_rope_store_workspace_size(8, 32, 8, 128, 4096, L.PGB_BF16) == \
+        lib.pgb_col_gemm_workspace_size(8, 6144, 4096)
+    assert lib.pgb_gate_up_silu_workspace_size(3, 16, 32, L.PGB_F32) == 256 + 8192 + 3 * 32 * 4
+    assert lib.pgb_comm_set_one_rank_path(None, 1) == L.PGB_ERR_INVALID
+
+
+def test_torch_ops_have_no_cpu_fallback(pgb):
+    """The new ops refuse CPU tensors loudly instead of computing on the host."""
+    import torch
+
+    x = torch.zeros(2, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        pgb.gate_up_silu(x, torch.zeros(32, 64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        pgb.silu_and_mul(x)
+    with pytest.raises(ValueError, match="CUDA"):
+        pgb.ops.qkv_rope_store(x, torch.zeros(3 * 128, 64, dtype=torch.bfloat16), torch.zeros(2, dtype=torch.int32),
+                               torch.zeros(2, dtype=torch.int32), torch.zeros(8, 128), 1, 1, 128,
+                               torch.zeros(4, 1, 128, dtype=torch.bfloat16), torch.zeros(4, 1, 128, dtype=torch.bfloat16))
