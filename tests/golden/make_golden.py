@@ -29,6 +29,10 @@ What it records:
              (include/flashinfer/activation.cuh, silu from
              flashinfer/jit/activation.py), checked against
              torch.nn.functional.silu before it is used.
+  layer_shapes.json  state-dict keys and shard shapes of the reference's
+             GatedMLP and RotaryAttention (config 2, TP 1/2/4/8, and a qwen-style
+             bias + kv-replication case), so the mirrors' drop-in shapes are
+             checked without the reference.
   rope_small.npz  the reference's RoPE cos/sin tables (get_rope,
              python/picosgl/layers/rotary.py:63-151) for default, partial
              (rotary_dim < head_dim), llama3 and yarn scaling. Applying them
@@ -289,10 +293,39 @@ def make_rope_small():
     np.savez_compressed(HERE / "rope_small.npz", **data)
 
 
+LAYER_CASES = {
+    "config2": dict(hidden=4096, inter=12288, head_dim=128, nq=32, nkv=8, bias=False),
+    "bias_kv2": dict(hidden=2048, inter=5632, head_dim=64, nq=16, nkv=2, bias=True),
+}
+
+
+def make_layer_shapes():
+    import json
+
+    (info, DistributedInfo, set_tp_info, _, _, _, _, _, _) = _ref_imports()
+    from picosgl.layers.attention import RotaryAttention
+    from picosgl.layers.mlp import GatedMLP
+
+    out = {}
+    for name, c in LAYER_CASES.items():
+        for n in (1, 2, 4, 8):
+            _reset_tp(info, DistributedInfo, set_tp_info, 0, n)
+            attn = RotaryAttention(c["hidden"], c["head_dim"], c["nq"], c["nkv"], 0, c["head_dim"], 256, 1e6, None,
+                                   has_attn_bias=c["bias"])
+            mlp = GatedMLP(c["hidden"], c["inter"], "silu")
+            out[f"{name}_tp{n}"] = {
+                "attn": {k: list(v.shape) for k, v in attn.state_dict().items()},
+                "mlp": {k: list(v.shape) for k, v in mlp.state_dict().items()},
+                "attn_local_heads": [attn.num_qo_heads, attn.num_kv_heads],
+            }
+    (HERE / "layer_shapes.json").write_text(json.dumps({"cases": LAYER_CASES, "shapes": out}, indent=1))
+
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
     make_tp_small()
     make_mlp_small()
     make_rope_small()
+    make_layer_shapes()
     make_cfg1()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))

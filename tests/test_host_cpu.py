@@ -204,3 +204,36 @@ def test_linked_row_layers_fuse_and_match_unfused(pgb, monkeypatch):
     # the row-parallel layer that produces its input.
     assert rec.calls == ["rmsnorm"] + ["row_fused"] * (2 * len(layers))
     torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_attention_and_mlp_mirrors_match_reference_shapes():
+    """RotaryAttention / GatedMLP mirrors: the reference's state-dict keys and
+    shard shapes at TP 1/2/4/8 (kv-head replication and attention bias
+    included), recorded from the reference by tests/golden/make_golden.py."""
+    import json
+
+    L = importlib.import_module("pico-sglang_b200.layers")
+    D = importlib.import_module("pico-sglang_b200.distributed")
+    gold = json.loads((Path(__file__).resolve().parent / "golden" / "layer_shapes.json").read_text())
+    for name, c in gold["cases"].items():
+        for n in (1, 2, 4, 8):
+            ref = gold["shapes"][f"{name}_tp{n}"]
+            with D.tp_override(D.DistributedInfo(0, n)):
+                attn = L.RotaryAttention(c["hidden"], c["head_dim"], c["nq"], c["nkv"], 0, c["head_dim"], 256, 1e6,
+                                         None, has_attn_bias=c["bias"])
+                mlp = L.GatedMLP(c["hidden"], c["inter"], "silu")
+            assert {k: list(v.shape) for k, v in attn.state_dict().items()} == ref["attn"], (name, n)
+            assert {k: list(v.shape) for k, v in mlp.state_dict().items()} == ref["mlp"], (name, n)
+            assert [attn.num_qo_heads, attn.num_kv_heads] == ref["attn_local_heads"]
+
+
+def test_gated_mlp_and_attention_refuse_unfused_variants():
+    L = importlib.import_module("pico-sglang_b200.layers")
+    D = importlib.import_module("pico-sglang_b200.distributed")
+    with D.tp_override(D.DistributedInfo(0, 1)):
+        with pytest.raises(NotImplementedError):
+            L.GatedMLP(64, 128, "gelu")
+        with pytest.raises(ValueError):
+            L.GatedMLP(64, 128, "relu")
+        with pytest.raises(NotImplementedError):
+            L.RotaryAttention(256, 64, 4, 1, 0, 64, 32, 1e4, None, qk_norm_eps=1e-6)
