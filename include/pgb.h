@@ -223,7 +223,8 @@ PGB_API int pgb_qkv_rope_store(const void* x, const void* w, const void* bias, i
 /* RoPE + KV-cache store from a materialised qkv [T, (nq + 2 nkv) hd] (same
  * layout, arithmetic and limits as pgb_qkv_rope_store): flashinfer's
  * apply_rope_with_cos_sin_cache_inplace (python/picosgl/layers/rotary.py:53-59)
- * followed by store_cache (python/picosgl/kernel/store.py:37-51). status is a
+ * followed by store_cache (python/picosgl/kernel/store.py:37-51). qkv, q_out
+ * and both caches are all of element type dtype. status is a
  * device int (the index-error word) set to 5 when a token is skipped for an
  * out-of-range index. */
 PGB_API int pgb_rope_store(const void* qkv, int T, int num_q_heads, int num_kv_heads, int head_dim,

@@ -221,6 +221,12 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, out_loc: torch.Tensor
                status: torch.Tensor | None = None) -> torch.Tensor:
     """RoPE + KV-cache store from a materialised qkv [T, (nq + 2 nkv) hd]
     (flashinfer apply_rope_with_cos_sin_cache_inplace + store_cache); returns q."""
+    # The kernel reads and writes every tensor in qkv's element type.
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache), ("q_out", q_out)):
+        if t is not None and t.dtype != qkv.dtype:
+            raise TypeError(f"{name} dtype {t.dtype} differs from qkv {qkv.dtype}")
+    if status is not None and (status.dtype != torch.int32 or status.numel() < 1):
+        raise TypeError("status must be a CUDA int32 tensor of at least one element")
     _require_cuda("qkv", qkv)
     nq, nkv, hd = num_q_heads, num_kv_heads, head_dim
     T = qkv.shape[0]
@@ -229,8 +235,14 @@ def rope_store(qkv: torch.Tensor, positions: torch.Tensor, out_loc: torch.Tensor
     rows = _rope_common(positions, out_loc, cos_sin_cache, k_cache, v_cache, T, nkv, hd)
     if q_out is None:
         q_out = torch.empty((T, nq * hd), dtype=qkv.dtype, device=qkv.device)
+    else:
+        _require_cuda("q_out", q_out)
+        if q_out.numel() != T * nq * hd:
+            raise ValueError("q_out must hold [T, nq * hd] elements")
     if status is None:
         status = torch.zeros(1, dtype=torch.int32, device=qkv.device)
+    else:
+        _require_cuda("status", status)
     _lib.call("pgb_rope_store", qkv.data_ptr(), T, nq, nkv, hd, cos_sin_cache.shape[1], positions.data_ptr(),
               out_loc.data_ptr(), _INDEX[positions.dtype], cos_sin_cache.data_ptr(), cos_sin_cache.shape[0],
               q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), rows, dtype_code(qkv), status.data_ptr(),

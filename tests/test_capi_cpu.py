@@ -157,3 +157,22 @@ def test_torch_ops_have_no_cpu_fallback(pgb):
         pgb.ops.qkv_rope_store(x, torch.zeros(3 * 128, 64, dtype=torch.bfloat16), torch.zeros(2, dtype=torch.int32),
                                torch.zeros(2, dtype=torch.int32), torch.zeros(8, 128), 1, 1, 128,
                                torch.zeros(4, 1, 128, dtype=torch.bfloat16), torch.zeros(4, 1, 128, dtype=torch.bfloat16))
+
+
+def test_rope_store_rejects_mixed_dtypes_before_launch(pgb):
+    """rope_store computes in qkv's element type end to end, so caches or a q
+    buffer of another type would be written past their rows: refused."""
+    import torch
+
+    qkv = torch.zeros(2, 3 * 128, dtype=torch.float32)
+    idx = torch.zeros(2, dtype=torch.int32)
+    table = torch.zeros(8, 128)
+    kc = torch.zeros(4, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(TypeError, match="k_cache"):
+        pgb.ops.rope_store(qkv, idx, idx, table, 1, 1, 128, kc, kc.float())
+    with pytest.raises(TypeError, match="q_out"):
+        pgb.ops.rope_store(qkv, idx, idx, table, 1, 1, 128, kc.float(), kc.float(),
+                           q_out=torch.zeros(2, 128, dtype=torch.bfloat16))
+    with pytest.raises(TypeError, match="status"):
+        pgb.ops.rope_store(qkv, idx, idx, table, 1, 1, 128, kc.float(), kc.float(),
+                           status=torch.zeros(1, dtype=torch.int64))
