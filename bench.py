@@ -13,7 +13,9 @@ LlamaDecoderLayer.forward (models/llama.py:77-86), built from this repo's
 public layer classes: qkv_proj (column GEMM) -> o_proj fused with the
 all-reduce and post_attention_layernorm -> gate_up_proj (column GEMM) on that
 norm's output -> down_proj fused with the all-reduce and the next layer's
-input_layernorm. Attention and silu_and_mul are outside the step; their
+input_layernorm. With one GPU there is no all-reduce, and each row-parallel
+layer runs as the column GEMM followed by the fused_add_rmsnorm kernel
+(`config.row_path`). Attention and silu_and_mul are outside the step; their
 outputs are fixed synthetic activations. The gated MLP's front half
 (gate_up_proj + silu_and_mul, fused by pgb_gate_up_silu) is timed beside the
 step under `config.mlp_front_us`, and the attention block's front (qkv_proj +
@@ -423,6 +425,8 @@ def run_ours(args) -> dict | None:
                 "workload": f"config 2 decode layer, T={T} tokens, TP={n}",
                 "hidden": H, "intermediate": I, "q_heads": NQ, "kv_heads": NKV, "head_dim": HD,
                 "tokens": T, "tp": n, "layers_per_step": n_layers,
+                "row_path": ("fused GEMM + all-reduce + residual-add + RMSNorm kernel" if n > 1 else
+                             "one rank: column GEMM then the fused_add_rmsnorm kernel (no all-reduce)"),
                 "l2": f"inputs larger than L2: {n_layers} distinct layers, "
                       f"{bytes_per_layer * n_layers / 2**20:.0f} MiB of weights per GPU per step",
                 "graph": "step captured in one CUDA graph and replayed",
