@@ -159,10 +159,21 @@ PGB_API int pgb_col_gemm(const void* x, const void* w, const void* bias, void* y
  *  - all calls on a device share it, so calls whose GPU work overlaps
  *    (unordered streams) race and give wrong results;
  *  - the first call on each device looks up the scratch address, so make it
- *    before any stream capture.
+ *    before any stream capture; the address is kept for the life of the
+ *    process, so do not use the library across a cudaDeviceReset;
+ *  - PGB_F32 (check mode) uses no scratch and has no size limit;
+ *  - a refused call (bad argument, size above the limit) does not touch the
+ *    scratch.
  * Arguments and results are those of pgb_col_gemm. */
 PGB_API int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bias, void* y, int T, int N,
                                  int K, int dtype, void* stream);
+
+/* Status word of pgb_col_gemm_noalloc on the current device: *out = PGB_OK,
+ * or PGB_ERR_TIMEOUT when a bounded device-side wait of an earlier call ran
+ * out (that call's output is then incomplete). The word is sticky across
+ * calls; reset != 0 clears it. Synchronises the device. No reference
+ * counterpart. */
+PGB_API int pgb_col_gemm_noalloc_status(int* out, int reset);
 
 /* gate_up_proj GEMM with silu_and_mul in its epilogue:
  *   gate_up  = x[T, K] . w[2I, K]^T (+ bias[2I]), rounded to dtype

@@ -76,6 +76,7 @@ _SIGS: dict[str, tuple[object, list[object]]] = {
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
     ),
+    "pgb_col_gemm_noalloc_status": (c_int, [POINTER(c_int), c_int]),
     "pgb_gate_up_silu_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
     "pgb_gate_up_silu": (
         c_int,

@@ -182,7 +182,11 @@ extern "C" int pgb_gate_up_silu(const void* x, const void* w, const void* bias, 
 //    workspace per stream.
 //  - The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current). Make that first call
-//    before any stream capture.
+//    before any stream capture. The address is kept for the life of the
+//    process, so the library must not be used across a cudaDeviceReset.
+//  - The kernel's status word sits in the array too and is sticky: a
+//    device-side wait that ran out leaves it set until
+//    pgb_col_gemm_noalloc_status reads and resets it.
 // ---------------------------------------------------------------------------
 
 static __device__ __align__(256) uint8_t pgb_noalloc_scratch[PGB_NOALLOC_SCRATCH_BYTES];
@@ -223,6 +227,18 @@ extern "C" int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bi
   if (T < 0 || N <= 0 || K <= 0)
     return set_error(PGB_ERR_INVALID, "col_gemm_noalloc: bad shape T=%d N=%d K=%d", T, N, K);
   if (T == 0) return PGB_OK;
+  // f32 check mode runs the CUDA-core GEMM, which uses no scratch at all.
+  if (dtype == PGB_F32) return pgb_col_gemm(x, w, bias, y, T, N, K, dtype, nullptr, 0, stream);
+  // Everything pgb_col_gemm would refuse is refused here first, so a refused
+  // call never touches the shared scratch.
+  if (dtype != PGB_BF16 && dtype != PGB_F16)
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm_noalloc: dtype %d not supported", dtype);
+  if (K % 8 != 0 || N % 8 != 0)
+    return set_error(PGB_ERR_INVALID, "col_gemm_noalloc: K=%d and N=%d must be multiples of 8", K, N);
+  if (x == nullptr || w == nullptr || y == nullptr)
+    return set_error(PGB_ERR_INVALID, "col_gemm_noalloc: null pointer argument");
+  if ((reinterpret_cast<uintptr_t>(y) & 15u) != 0u)
+    return set_error(PGB_ERR_INVALID, "col_gemm_noalloc: output is not 16-byte aligned");
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc) return rc;
@@ -236,11 +252,27 @@ extern "C" int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bi
   uint8_t* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  // The status word and the split-tile counters must start at zero; the
-  // exchange area behind them is written before it is read.
+  // The split-tile counters must start at zero; the exchange area behind
+  // them is written before it is read. The status word in the header is left
+  // alone: it stays set after a device-side wait ran out, until
+  // pgb_col_gemm_noalloc_status resets it.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  PGB_CUDA_TRY(cudaMemsetAsync(scratch, 0, kWsHeaderBytes + kWsCounterBytes, s));
+  PGB_CUDA_TRY(cudaMemsetAsync(scratch + kWsHeaderBytes, 0, kWsCounterBytes, s));
   return pgb_col_gemm(x, w, bias, y, T, N, K, dtype, scratch, PGB_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+extern "C" int pgb_col_gemm_noalloc_status(int* out, int reset) {
+  using namespace pgb;
+  if (out == nullptr) return set_error(PGB_ERR_INVALID, "col_gemm_noalloc_status: null output");
+  uint8_t* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  PGB_CUDA_TRY(cudaDeviceSynchronize());
+  int v = 0;
+  PGB_CUDA_TRY(cudaMemcpy(&v, scratch, sizeof(int), cudaMemcpyDeviceToHost));
+  *out = v == kDevOk ? PGB_OK : (v == kDevBadArgs ? PGB_ERR_INVALID : PGB_ERR_TIMEOUT);
+  if (reset) PGB_CUDA_TRY(cudaMemset(scratch, 0, sizeof(int)));
+  return PGB_OK;
 }
 
 #ifdef PGB_TRACE

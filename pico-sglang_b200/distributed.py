@@ -16,6 +16,7 @@
 from __future__ import annotations
 
 import ctypes
+import sys
 from abc import ABC, abstractmethod
 from contextlib import contextmanager
 from dataclasses import dataclass
@@ -27,49 +28,65 @@ from . import _lib
 from .ops import _require_cuda, _stream, dtype_code
 
 # ------------------------------------------------------------------ TP info --
+# The tensor-parallel rank and size, process-wide. Same names and meaning as
+# the reference's distributed/info.py:7-46 (DistributedInfo, set_tp_info,
+# get_tp_info, try_get_tp_info, tp_override) so layer code written against
+# those names runs unchanged. When this package runs inside the reference's
+# process and only the reference's own module holds the TP info, the lookups
+# below read it from there, so the two cannot disagree.
 
 
 @dataclass(frozen=True)
 class DistributedInfo:
-    """Rank and size of the tensor-parallel group (distributed/info.py:7-16)."""
+    """Rank and size of the tensor-parallel group."""
 
     rank: int
     size: int
 
     def __post_init__(self):
-        assert 0 <= self.rank < self.size
+        if not (self.size >= 1 and 0 <= self.rank < self.size):
+            raise AssertionError(f"rank {self.rank} outside a TP group of {self.size}")
 
     def is_primary(self) -> bool:
         return self.rank == 0
 
 
-_TP_INFO: DistributedInfo | None = None
+class _TPState:
+    current: DistributedInfo | None = None
+
+
+def _reference_tp_info():
+    mod = sys.modules.get("picosgl.distributed.info")
+    getter = getattr(mod, "try_get_tp_info", None) if mod is not None else None
+    info = getter() if getter is not None else None
+    return None if info is None else DistributedInfo(int(info.rank), int(info.size))
 
 
 def set_tp_info(tp_info: DistributedInfo) -> None:
-    global _TP_INFO
-    assert _TP_INFO is None, "TP info has been set"
-    _TP_INFO = tp_info
-
-
-def get_tp_info() -> DistributedInfo:
-    assert _TP_INFO is not None, "TP info has not been set"
-    return _TP_INFO
+    if _TPState.current is not None:
+        raise AssertionError("the TP info is already set for this process")
+    _TPState.current = tp_info
 
 
 def try_get_tp_info() -> DistributedInfo | None:
-    return _TP_INFO
+    return _TPState.current if _TPState.current is not None else _reference_tp_info()
+
+
+def get_tp_info() -> DistributedInfo:
+    info = try_get_tp_info()
+    if info is None:
+        raise AssertionError("the TP info has not been set (call set_tp_info first)")
+    return info
 
 
 @contextmanager
 def tp_override(tp_info: DistributedInfo):
-    global _TP_INFO
-    saved = _TP_INFO
-    _TP_INFO = tp_info
+    """Temporarily replace the TP info (restored on exit, errors included)."""
+    before, _TPState.current = _TPState.current, tp_info
     try:
         yield
     finally:
-        _TP_INFO = saved
+        _TPState.current = before
 
 
 # ------------------------------------------------------------- communicator --

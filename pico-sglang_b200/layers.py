@@ -33,42 +33,51 @@ from .distributed import DistributedCommunicator, get_tp_info, local_comm
 
 
 def div_even(a: int, b: int, allow_replicate: bool = False) -> int:
-    """utils/misc.py:20-26."""
-    if allow_replicate and b > a:
-        assert b % a == 0, f"{b = } must be divisible by {a = } for KV head replication"
+    """a / b for an exact split across b ranks (the contract of utils/misc.py:20-26).
+
+    With allow_replicate, fewer items than ranks (kv heads under a wide TP
+    group) give 1 item per rank, each replicated on b / a ranks."""
+    if allow_replicate and a < b:
+        if b % a:
+            raise AssertionError(f"{b} ranks cannot replicate {a} kv heads evenly")
         return 1
-    assert a % b == 0, f"{a = } must be divisible by {b = }"
-    return a // b
+    q, rem = divmod(a, b)
+    if rem:
+        raise AssertionError(f"{a} does not split evenly over {b} ranks")
+    return q
+
+
+def _public_attrs(obj):
+    return [(k, v) for k, v in vars(obj).items() if not k.startswith("_")]
 
 
 class BaseOP:
-    """Attribute-walking state dict of layers/base.py:14-59."""
+    """Loader contract of layers/base.py:14-59: every public tensor attribute is
+    a parameter named by its attribute path ("mlp.down_proj.weight"); nested
+    BaseOPs contribute their own under their attribute name."""
 
     def state_dict(self, *, prefix: str = "", result: dict | None = None) -> dict:
-        result = result if result is not None else {}
-        for name, param in self.__dict__.items():
-            if name.startswith("_"):
-                continue
-            key = f"{prefix}.{name}" if prefix else name
-            if isinstance(param, torch.Tensor):
-                result[key] = param
-            elif isinstance(param, BaseOP):
-                param.state_dict(prefix=key, result=result)
-        return result
+        out = {} if result is None else result
+        for name, val in _public_attrs(self):
+            path = name if not prefix else prefix + "." + name
+            if isinstance(val, BaseOP):
+                val.state_dict(prefix=path, result=out)
+            elif isinstance(val, torch.Tensor):
+                out[path] = val
+        return out
 
     def load_state_dict(self, state_dict: dict, *, prefix: str = "", _internal: bool = False) -> None:
-        for name, param in self.__dict__.items():
-            if name.startswith("_"):
-                continue
-            key = f"{prefix}.{name}" if prefix else name
-            if isinstance(param, torch.Tensor):
-                item = state_dict.pop(key)
-                assert param.shape == item.shape, f"shape mismatch for {key}: {param.shape} vs {item.shape}"
-                setattr(self, name, item.to(param.dtype))
-            elif isinstance(param, BaseOP):
-                param.load_state_dict(state_dict, prefix=key, _internal=True)
-        if not _internal and state_dict:
-            raise RuntimeError(f"Unexpected keys in state_dict: {list(state_dict.keys())}")
+        for name, val in _public_attrs(self):
+            path = name if not prefix else prefix + "." + name
+            if isinstance(val, BaseOP):
+                val.load_state_dict(state_dict, prefix=path, _internal=True)
+            elif isinstance(val, torch.Tensor):
+                new = state_dict.pop(path)
+                if tuple(new.shape) != tuple(val.shape):
+                    raise AssertionError(f"{path}: checkpoint shape {tuple(new.shape)}, layer {tuple(val.shape)}")
+                setattr(self, name, new.to(val.dtype))
+        if state_dict and not _internal:
+            raise RuntimeError(f"Unexpected keys in state_dict: {sorted(state_dict)}")
 
 
 class _FuseContext(threading.local):

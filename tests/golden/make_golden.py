@@ -1,10 +1,11 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Runs in the build container only (it imports the reference read-only from
-its source tree; set PICOSGL_SRC if it is not at the default path). The
-fixtures it writes are committed, so the tests never need the reference.
+Runs only where the reference's Python sources are present: it imports them
+read-only from the directory that PICOSGL_SRC names (the reference project's
+`python/` directory). The fixtures it writes are committed, so the tests never
+need the reference.
 
-    python tests/golden/make_golden.py
+    PICOSGL_SRC=<reference checkout>/python python tests/golden/make_golden.py
 
 What it records:
   cfg1.npz   BASELINE config 1 (CPU plumbing): the reference's
@@ -52,10 +53,12 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 HERE = Path(__file__).resolve().parent
-REF = os.environ.get("PICOSGL_SRC", "/root/reference/python")
+REF = os.environ.get("PICOSGL_SRC", "")
 
 
 def _ref_imports():
+    if not REF:
+        raise SystemExit("set PICOSGL_SRC to the reference project's python/ directory")
     if REF not in sys.path:
         sys.path.insert(0, REF)
     import picosgl.distributed.info as info  # noqa: F401

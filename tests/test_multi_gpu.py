@@ -133,12 +133,13 @@ def _worker(rank: int, world: int, port: int, case: str, q):
                 out[f"y_{T}_{H}_{K}"] = _within(yy, y)
                 out[f"exact_out_{T}_{H}_{K}"] = _no_worse_than_reference(o, ref, exact)
                 out[f"exact_res_{T}_{H}_{K}"] = _no_worse_than_reference(rr, ref_r, se)
-                # Every rank must hold the identical result (replicated residual stream).
-                gathered = [torch.empty_like(o) for _ in range(world)]
-                objs = [None] * world
-                dist.all_gather_object(objs, (o.float().sum().item(), rr.float().sum().item()))
-                out[f"same_{T}_{H}_{K}"] = (len(set(objs)) == 1, str(objs))
-                del gathered
+                # Every rank must hold the identical result (replicated residual
+                # stream): gather every rank's tensors and compare them bit for bit.
+                mine = torch.cat([o.reshape(-1), rr.reshape(-1), yy.reshape(-1)]).view(torch.uint8).cpu()
+                gathered = [torch.empty_like(mine) for _ in range(world)]
+                dist.all_gather(gathered, mine)
+                same = all(torch.equal(gathered[0], t) for t in gathered[1:])
+                out[f"same_{T}_{H}_{K}"] = (same, "tensors differ between ranks")
             # f32 check mode: IEEE f32 GEMM + all-reduce + add/RMSNorm, 1e-5 relative
             T, H, K = 8, 4096, 4096
             g = torch.Generator(device=dev).manual_seed(17)
