@@ -402,6 +402,14 @@ extern "C" int pgb_comm_set_one_rank_path(pgb_comm* comm, int fused) {
   return PGB_OK;
 }
 
+extern "C" int pgb_comm_set_exchange_mode(pgb_comm* comm, int mode) {
+  if (comm == nullptr) return set_error(PGB_ERR_INVALID, "set_exchange_mode: null communicator");
+  if (mode < PGB_XCHG_AUTO || mode > PGB_XCHG_BARRIER)
+    return set_error(PGB_ERR_INVALID, "set_exchange_mode: unknown mode %d", mode);
+  comm->exchange_mode = mode;
+  return PGB_OK;
+}
+
 extern "C" int pgb_comm_get_status(pgb_comm* comm, int* out, int reset) {
   if (comm == nullptr || out == nullptr) return set_error(PGB_ERR_INVALID, "get_status: null argument");
   DeviceGuard g(comm->device);

@@ -6,6 +6,9 @@
 //   [header 4 KB]  magic, uid, world size, layout sizes (checked by peers)
 //   [flags  4 KB]  flags[bar][src_rank]: epoch written by src when it passed
 //                  cross-rank barrier `bar`
+//   [piece flags 2 x 32 KB]  per-piece arrival flags of the exchange kernel
+//                  (row_xchg.cu): rs[src_rank][cta] and ag[owner_rank][cta],
+//                  each (epoch << 8 | pieces delivered by that CTA)
 //   [user buffer]  max_bytes, returned by get_buffer
 //   [slots  x 2]   two parities of partial rows pushed by the ranks:
 //                  slot[src_rank][row][width]
@@ -32,8 +35,11 @@ namespace pgb {
 
 constexpr int kNumBars = 4;          // flags per rank: barrier ids 0..3
 constexpr size_t kHeaderBytes = 4096;
-constexpr size_t kFlagBytes = 4096;
-constexpr uint64_t kCommMagic = 0x3030324247504255ull;  // layout tag
+constexpr size_t kBarFlagBytes = 4096;
+constexpr int kXchgMaxCtas = 1024;   // piece-flag rows are this many CTAs wide
+constexpr size_t kXchgFlagBytes = static_cast<size_t>(PGB_MAX_RANKS) * kXchgMaxCtas * 4u;
+constexpr size_t kFlagBytes = kBarFlagBytes + 2 * kXchgFlagBytes;
+constexpr uint64_t kCommMagic = 0x3130324247504255ull;  // layout tag
 constexpr size_t kSplitScratchBytes = 32u << 20;        // split-tile exchange area per comm
 constexpr size_t kTileCounterBytes = 64u << 10;
 
@@ -64,7 +70,7 @@ struct CommDev {
   int world;
   uint8_t* slots[PGB_MAX_RANKS];    // slot region base (parity 0) of each rank
   uint8_t* results[PGB_MAX_RANKS];  // result region base (parity 0) of each rank
-  uint32_t* flags[PGB_MAX_RANKS];   // flag area of each rank
+  uint32_t* flags[PGB_MAX_RANKS];   // flag area of each rank (barrier flags, then the piece flags)
   uint64_t slot_parity_bytes;
   uint64_t result_parity_bytes;
   uint32_t* epoch;
@@ -72,6 +78,15 @@ struct CommDev {
   int* status;
   uint64_t timeout_ns;
 };
+
+// Piece flags of rank `d` (see the layout above): reduce-scatter arrivals
+// rs[src][cta] and all-gather arrivals ag[owner][cta].
+__host__ __device__ inline uint32_t* xchg_rs_flags(const CommDev& cm, int d) {
+  return cm.flags[d] + kBarFlagBytes / 4;
+}
+__host__ __device__ inline uint32_t* xchg_ag_flags(const CommDev& cm, int d) {
+  return cm.flags[d] + (kBarFlagBytes + kXchgFlagBytes) / 4;
+}
 
 }  // namespace pgb
 
@@ -91,6 +106,7 @@ struct pgb_comm {
   uint64_t timeout_ns;
   int sm_count;
   int one_rank_fused = 0;  // world == 1: run the row op as the fused kernel (else GEMM + norm)
+  int exchange_mode = PGB_XCHG_AUTO;  // multi-rank decode row ops, see pgb_comm_set_exchange_mode
 };
 
 namespace pgb {

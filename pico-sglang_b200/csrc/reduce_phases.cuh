@@ -233,16 +233,17 @@ __device__ __forceinline__ void unpack8_io(const uint4& u, float* v) {
 // and norm-weight vectors together; the f32 pre-norm row and the weights wait
 // in shared memory `srow` (width f32 + width IO values) for the second pass,
 // which only reads shared memory and stores. IO is 16-bit.
+//
+// reduce_row_src is the same for an explicit source: row t's nsrc partial rows
+// start at slot0, src_stride elements apart; push sends the finished rows to
+// every peer's result region (two-shot owners of row_fused.cu).
 template <typename IO, int MAXV>
-__device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity, int t, int width,
-                                        IO* out, IO* residual, const IO* norm_w, float eps, int do_norm, float* red,
-                                        float* srow) {
+__device__ __forceinline__ void reduce_row_src(const CommDev& cm, uint32_t parity, const IO* slot0,
+                                               size_t src_stride, int nsrc, bool push, int t, int width, IO* out,
+                                               IO* residual, const IO* norm_w, float eps, int do_norm, float* red,
+                                               float* srow) {
   static_assert(sizeof(IO) == 2, "16-bit I/O");
   const int nvec = width >> 3;
-  const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
-  const IO* slot0 = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes) +
-                    static_cast<size_t>(lr) * width;
-  const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
   uint4* wrow = reinterpret_cast<uint4*>(srow + width);
   const size_t row_off = static_cast<size_t>(t) * width;
   float ss = 0.f;
@@ -259,11 +260,11 @@ __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs
     uint4 sv[PGB_MAX_RANKS];
 #pragma unroll
     for (int d = 0; d < PGB_MAX_RANKS; ++d)
-      if (d < cm.world) sv[d] = __ldcg(reinterpret_cast<const uint4*>(slot0 + d * src_stride) + v);
+      if (d < nsrc) sv[d] = __ldcg(reinterpret_cast<const uint4*>(slot0 + d * src_stride) + v);
     unpack8_io<IO>(sv[0], s8);
 #pragma unroll
     for (int d = 1; d < PGB_MAX_RANKS; ++d) {
-      if (d < cm.world) {
+      if (d < nsrc) {
         unpack8_io<IO>(sv[d], p);
 #pragma unroll
         for (int j = 0; j < 8; ++j) s8[j] += p[j];
@@ -287,7 +288,6 @@ __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs
   float rcp = 1.f;
   if (do_norm) rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
   else __syncthreads();
-  const bool push = !rs.oneshot && cm.world > 1;
 #pragma unroll 1
   for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
     const float4 a = reinterpret_cast<const float4*>(srow)[2 * v];
@@ -319,6 +319,17 @@ __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs
   __syncthreads();
 }
 
+template <typename IO, int MAXV>
+__device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs, uint32_t parity, int t, int width,
+                                        IO* out, IO* residual, const IO* norm_w, float eps, int do_norm, float* red,
+                                        float* srow) {
+  const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
+  const IO* slot0 = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes) +
+                    static_cast<size_t>(lr) * width;
+  reduce_row_src<IO, MAXV>(cm, parity, slot0, static_cast<size_t>(rs.rows_cap) * width, cm.world,
+                           !rs.oneshot && cm.world > 1, t, width, out, residual, norm_w, eps, do_norm, red, srow);
+}
+
 // Phase 2 with one warp per row, for launches with more rows than CTAs
 // (prefill, and wide decode batches): every warp of the grid reduces its own
 // rows, so rows proceed in parallel instead of one after another per CTA.
@@ -327,10 +338,15 @@ __device__ __forceinline__ void reduce_row(const CommDev& cm, const RowSplit& rs
 // slice of `stage` (width * 4 bytes per warp), the norm weights are staged
 // once per CTA after those slices; the sum of squares is reduced with
 // shuffles. Called by every thread of the CTA. IO is 16-bit.
-template <typename IO>
-__device__ __forceinline__ void reduce_rows_warp(const CommDev& cm, const RowSplit& rs, uint32_t parity, int r0,
-                                                 int r1, int width, IO* out, IO* residual, const IO* norm_w,
-                                                 float eps, int do_norm, uint8_t* stage) {
+//
+// reduce_rows_warp_src takes the sources explicitly: src0(t) is row t of
+// source 0, the nsrc sources src_stride elements apart; push as in
+// reduce_row_src.
+template <typename IO, typename Src0>
+__device__ __forceinline__ void reduce_rows_warp_src(const CommDev& cm, uint32_t parity, Src0&& src0,
+                                                     size_t src_stride, int nsrc, bool push, int r0, int r1,
+                                                     int width, IO* out, IO* residual, const IO* norm_w, float eps,
+                                                     int do_norm, uint8_t* stage) {
   static_assert(sizeof(IO) == 2, "16-bit I/O");
   constexpr int kBatch = 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -343,16 +359,12 @@ __device__ __forceinline__ void reduce_rows_warp(const CommDev& cm, const RowSpl
     for (int v = threadIdx.x; v < nvec; v += blockDim.x) wrow[v] = __ldg(reinterpret_cast<const uint4*>(norm_w) + v);
   }
   __syncthreads();
-  const size_t src_stride = static_cast<size_t>(rs.rows_cap) * width;
-  const bool push = !rs.oneshot && cm.world > 1;
 #pragma unroll 1
   // Rows go to CTAs first, then to warps: the rows spread over every SM
   // instead of filling a few SMs six warps deep.
   for (int t = r0 + warp * static_cast<int>(gridDim.x) + static_cast<int>(blockIdx.x); t < r1;
        t += gridDim.x * nwarps) {
-    const int lr = rs.oneshot ? t : t - rs.first(cm.rank);
-    const IO* slot0 = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes) +
-                      static_cast<size_t>(lr) * width;
+    const IO* slot0 = src0(t);
     const size_t row_off = static_cast<size_t>(t) * width;
     float ss = 0.f;
 #pragma unroll 1
@@ -369,7 +381,7 @@ __device__ __forceinline__ void reduce_rows_warp(const CommDev& cm, const RowSpl
 #pragma unroll
       for (int b = 0; b < kBatch; ++b) unpack8_io<IO>(sv[b], acc[b]);
 #pragma unroll 1
-      for (int d = 1; d < cm.world; ++d) {
+      for (int d = 1; d < nsrc; ++d) {
 #pragma unroll
         for (int b = 0; b < kBatch; ++b)
           sv[b] = __ldcg(reinterpret_cast<const uint4*>(slot0 + d * src_stride) + min(v0 + 32 * b, nvec - 1));
@@ -433,6 +445,20 @@ __device__ __forceinline__ void reduce_rows_warp(const CommDev& cm, const RowSpl
     }
     __syncwarp();  // srow is reused by this warp's next row
   }
+}
+
+template <typename IO>
+__device__ __forceinline__ void reduce_rows_warp(const CommDev& cm, const RowSplit& rs, uint32_t parity, int r0,
+                                                 int r1, int width, IO* out, IO* residual, const IO* norm_w,
+                                                 float eps, int do_norm, uint8_t* stage) {
+  const IO* slots = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes);
+  const int first = rs.first(cm.rank);
+  const bool oneshot = rs.oneshot != 0;
+  reduce_rows_warp_src<IO>(
+      cm, parity,
+      [&](int t) { return slots + static_cast<size_t>(oneshot ? t : t - first) * width; },
+      static_cast<size_t>(rs.rows_cap) * width, cm.world, !rs.oneshot && cm.world > 1, r0, r1, width, out,
+      residual, norm_w, eps, do_norm, stage);
 }
 
 // Phase 3 (two-shot): copy the rows owned by other ranks from this rank's

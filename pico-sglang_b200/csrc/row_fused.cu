@@ -383,6 +383,9 @@ int row_f32(pgb_comm* comm, const void* x_local, const void* w_local, const void
   return rc;
 }
 
+int row_xchg(pgb_comm* comm, const void* x_local, const void* w_local, const void* bias, void* residual,
+             const void* norm_w, float eps, void* out, int T, int N, int K_local, int dtype, void* stream);
+
 // Choose one-shot or two-shot for a reduction of `rows` x `width` elements of
 // `elem` bytes; returns false if neither fits the communicator buffers.
 bool plan_rows(const pgb_comm* c, int rows, int width, int elem, RowSplit* rs) {
@@ -462,11 +465,28 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
     return pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, dtype, stream);
   }
 
+  if (comm->exchange_mode != PGB_XCHG_BARRIER) {
+    // Decode shapes: the per-piece exchange kernel (row_xchg.cu).
+    const int rc = row_xchg(comm, x_local, w_local, bias, residual, norm_w, eps, out, T, N, K_local, dtype, stream);
+    if (rc != PGB_ERR_UNSUPPORTED) return rc;
+  }
   RowSplit rs;
-  if (!plan_rows(comm, T, N, 2, &rs))
-    return set_error(PGB_ERR_INVALID,
-                     "row_gemm: %d x %d payload exceeds the communicator buffer (max_bytes=%zu)", T,
-                     N, comm->max_bytes);
+  if (!plan_rows(comm, T, N, 2, &rs)) {
+    // The payload does not fit the communicator's buffers (the reference
+    // then all-reduces in place, csrc/src/pynccl.cu:127-135): the GEMM into
+    // out, the chunked all-reduce over it, then the fused add + RMSNorm.
+    ColScratch sc;
+    sc.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
+    sc.ctr = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kCounters);
+    sc.ctr_bytes = kTileCounterBytes;
+    sc.xchg = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
+    sc.xchg_bytes = kSplitScratchBytes;
+    int rc = col_gemm_on_scratch(x_local, w_local, bias, out, T, N, K_local, dtype, sc, stream);
+    if (rc) return rc;
+    rc = pgb_all_reduce(comm, out, static_cast<size_t>(T) * N, dtype, PGB_OP_SUM, stream);
+    if (rc || norm_w == nullptr) return rc;
+    return pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, dtype, stream);
+  }
   const GemmPlan p = plan_gemm(T, N, K_local, comm->sm_count, kSplitScratchBytes);
   if (p.counter_bytes > kTileCounterBytes)
     return set_error(PGB_ERR_UNSUPPORTED, "row_gemm: too many split tiles (%d)", p.tiles - p.split_first);

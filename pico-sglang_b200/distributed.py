@@ -162,6 +162,15 @@ class PGBCommunicator:
         column GEMM followed by fused_add_rmsnorm (False, the default)."""
         _lib.call("pgb_comm_set_one_rank_path", self._h, int(bool(fused)))
 
+    def set_exchange_mode(self, mode: str) -> None:
+        """Multi-rank decode row ops: "auto" (default), "oneshot", "twoshot"
+        (per-piece exchange kernel) or "barrier" (the grid-barrier kernel)."""
+        codes = {"auto": _lib.PGB_XCHG_AUTO, "oneshot": _lib.PGB_XCHG_ONESHOT, "twoshot": _lib.PGB_XCHG_TWOSHOT,
+                 "barrier": _lib.PGB_XCHG_BARRIER}
+        if mode not in codes:
+            raise ValueError(f"unknown exchange mode {mode!r}; expected one of {sorted(codes)}")
+        _lib.call("pgb_comm_set_exchange_mode", self._h, codes[mode])
+
     # -- health -------------------------------------------------------------
     def set_timeout(self, seconds: float) -> None:
         _lib.call("pgb_comm_set_timeout_ns", self._h, int(seconds * 1e9))

@@ -104,8 +104,15 @@ def _worker(rank: int, world: int, port: int, case: str, q):
             out["gather"] = bool(torch.equal(dst, exp))
             comm.check_status()
         elif case == "fused":
-            for (T, H, K) in ((1, 4096, 4096), (8, 4096, 12288), (64, 4096, 4096), (256, 4096, 12288),
-                              (1000, 4096, 2048), (3, 200, 256)):
+            # Decode shapes under every exchange mode of the multi-rank row op
+            # (per-piece one-shot / two-shot, the cost model's pick, and the
+            # grid-barrier kernel), then a prefill shape and a ragged one.
+            runs = [(mode, shp) for mode in ("auto", "oneshot", "twoshot", "barrier")
+                    for shp in ((1, 4096, 4096), (8, 4096, 12288), (64, 4096, 4096), (256, 4096, 12288),
+                                (64, 5120, 25600))]
+            runs += [("auto", (1000, 4096, 2048)), ("auto", (3, 200, 256)), ("twoshot", (3, 200, 256))]
+            for mode, (T, H, K) in runs:
+                comm.set_exchange_mode(mode)
                 g = torch.Generator(device=dev).manual_seed(T + H + K)
                 x = torch.randn(T, K, device=dev, generator=g).bfloat16()
                 w = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
@@ -128,18 +135,20 @@ def _worker(rank: int, world: int, port: int, case: str, q):
                 o = pgb.ops.row_gemm_allreduce_addnorm(comm, xl, wl, rr, nw, EPS)
                 yy = pgb.ops.row_gemm_allreduce_addnorm(comm, xl, wl, None, None, EPS)
                 comm.check_status()
-                out[f"out_{T}_{H}_{K}"] = _within(o, ref)
-                out[f"res_{T}_{H}_{K}"] = _within(rr, ref_r)
-                out[f"y_{T}_{H}_{K}"] = _within(yy, y)
-                out[f"exact_out_{T}_{H}_{K}"] = _no_worse_than_reference(o, ref, exact)
-                out[f"exact_res_{T}_{H}_{K}"] = _no_worse_than_reference(rr, ref_r, se)
+                tag = f"{mode}_{T}_{H}_{K}"
+                out[f"out_{tag}"] = _within(o, ref)
+                out[f"res_{tag}"] = _within(rr, ref_r)
+                out[f"y_{tag}"] = _within(yy, y)
+                out[f"exact_out_{tag}"] = _no_worse_than_reference(o, ref, exact)
+                out[f"exact_res_{tag}"] = _no_worse_than_reference(rr, ref_r, se)
                 # Every rank must hold the identical result (replicated residual
                 # stream): gather every rank's tensors and compare them bit for bit.
                 mine = torch.cat([o.reshape(-1), rr.reshape(-1), yy.reshape(-1)]).view(torch.uint8).cpu()
                 gathered = [torch.empty_like(mine) for _ in range(world)]
                 dist.all_gather(gathered, mine)
                 same = all(torch.equal(gathered[0], t) for t in gathered[1:])
-                out[f"same_{T}_{H}_{K}"] = (same, "tensors differ between ranks")
+                out[f"same_{tag}"] = (same, "tensors differ between ranks")
+            comm.set_exchange_mode("auto")
             # f32 check mode: IEEE f32 GEMM + all-reduce + add/RMSNorm, 1e-5 relative
             T, H, K = 8, 4096, 4096
             g = torch.Generator(device=dev).manual_seed(17)
