@@ -232,8 +232,11 @@ PGB_API int pgb_silu_and_mul(const void* x, void* out, int T, int I, int dtype, 
  * store_kv (mha_pool.py:45-56 -> csrc/jit/store.cu:25-58). positions /
  * out_loc: [T] of index_dtype (PGB_I32 or PGB_I64). A token whose position or
  * slot is out of range is not written and sets the workspace's second int
- * (byte offset 4, the index-error word) to 5; the caller reads and clears it. head_dim 64 or 128; rotary_dim a multiple of 64 up to
- * head_dim; K % 8 == 0; q_out, caches and cos_sin_cache 16-byte aligned.
+ * (byte offset 4, the index-error word) to 5; the caller reads and clears it.
+ * head_dim 64, 128, 256 or 512 (rotary.py:49; 64 and 128 rotate in the GEMM
+ * epilogue, wider heads span several tiles and run the GEMM into the
+ * workspace followed by pgb_rope_store's kernel); rotary_dim a multiple of 64
+ * up to head_dim; K % 8 == 0; q_out, caches and cos_sin_cache 16-byte aligned.
  * dtype PGB_BF16 / PGB_F16, or PGB_F32 (check mode: f32 GEMM into the
  * workspace, then pgb_rope_store). workspace: at least
  * pgb_qkv_rope_store_workspace_size(...) bytes, zero-filled once; it may be

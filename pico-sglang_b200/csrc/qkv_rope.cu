@@ -20,9 +20,14 @@
 // in f32 on the values rounded to the model dtype (the reference
 // materialises qkv), rounded once. Dims rd .. hd stay as they are.
 //
-// Shapes: head_dim 64 or 128 (a 128-row decode tile then holds whole heads,
-// so every partner row is in the tile), rotary_dim a multiple of 64 up to
-// head_dim (partner chunks of the prefill epilogue stay 32-column aligned).
+// Shapes: head_dim 64, 128, 256 or 512 (the reference's RotaryEmbedding
+// accepts these, python/picosgl/layers/rotary.py:49), rotary_dim a multiple of
+// 64 up to head_dim (partner chunks of the prefill epilogue stay 32-column
+// aligned). With head_dim 64 or 128 a 128-row decode tile holds whole heads,
+// so every partner row is in the tile, and the rotation runs in the GEMM
+// epilogue. Wider heads span several tiles: the GEMM then writes qkv into the
+// workspace and the standalone RoPE + store kernel follows (two launches, the
+// same arithmetic).
 // An out-of-range position or cache slot skips that token and sets an
 // index-error word (kDevBadIndex) instead of writing out of bounds. That word
 // is not the workspace status word: the split-tile waits poll the status word
@@ -318,8 +323,8 @@ int rope_args(int T, int nq, int nkv, int hd, int rd, const void* positions, con
   if (T < 0 || nq <= 0 || nkv <= 0 || max_pos <= 0 || cache_rows < 0 || cache_rows > 0x7fffffffLL)
     return set_error(PGB_ERR_INVALID, "rope: bad sizes T=%d nq=%d nkv=%d max_pos=%d cache_rows=%lld", T, nq, nkv,
                      max_pos, cache_rows);
-  if (hd != 64 && hd != 128)
-    return set_error(PGB_ERR_UNSUPPORTED, "rope: head_dim %d (64 or 128 supported)", hd);
+  if (hd != 64 && hd != 128 && hd != 256 && hd != 512)
+    return set_error(PGB_ERR_UNSUPPORTED, "rope: head_dim %d (64, 128, 256 or 512 supported)", hd);
   if (rd <= 0 || rd > hd || rd % 64 != 0)
     return set_error(PGB_ERR_UNSUPPORTED, "rope: rotary_dim %d (a multiple of 64 up to head_dim)", rd);
   if (index_dtype != PGB_I32 && index_dtype != PGB_I64)
@@ -359,6 +364,12 @@ RopeStore<IO> make_rs(void* q, void* kc, void* vc, const void* positions, const 
 
 size_t f32_qkv_bytes(int T, int N) { return static_cast<size_t>(T) * static_cast<size_t>(N) * 4u; }
 
+// Heads too wide for the fused epilogue (see the file comment).
+bool rope_in_epilogue(int hd) { return hd <= kTileP; }
+
+// Wide heads: [column workspace | qkv T x N of the I/O type, 256-byte aligned].
+size_t wide_qkv_offset(const GemmPlan& p) { return align_up(col_workspace_bytes(p), 256); }
+
 int sm_count_or_148() {
   DeviceInfo d;
   if (current_device_info(&d) == PGB_OK) return d.sm_count;
@@ -374,7 +385,9 @@ extern "C" size_t pgb_qkv_rope_store_workspace_size(int T, int num_q_heads, int 
   const int N = (num_q_heads + 2 * num_kv_heads) * head_dim;
   if (T <= 0 || N <= 0 || K <= 0) return kWsHeaderBytes + kWsCounterBytes;
   if (dtype == PGB_F32) return kWsHeaderBytes + kWsCounterBytes + f32_qkv_bytes(T, N);
-  return col_workspace_bytes(plan_gemm(T, N, K, sm_count_or_148(), SIZE_MAX));
+  const GemmPlan p = plan_gemm(T, N, K, sm_count_or_148(), SIZE_MAX);
+  if (!rope_in_epilogue(head_dim)) return wide_qkv_offset(p) + f32_qkv_bytes(T, N) / 2;
+  return col_workspace_bytes(p);
 }
 
 extern "C" int pgb_qkv_rope_store(const void* x, const void* w, const void* bias, int T, int K, int num_q_heads,
@@ -419,9 +432,32 @@ extern "C" int pgb_qkv_rope_store(const void* x, const void* w, const void* bias
   rc = current_device_info(&dev);
   if (rc) return rc;
   const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, SIZE_MAX);
-  const size_t need = col_workspace_bytes(p);
+  const bool fused = rope_in_epilogue(hd);
+  const size_t need = fused ? col_workspace_bytes(p) : wide_qkv_offset(p) + f32_qkv_bytes(T, N) / 2;
   if (workspace_bytes < need)
     return set_error(PGB_ERR_INVALID, "qkv_rope_store: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+  if (!fused) {
+    // Wide heads: qkv into the workspace, then the standalone RoPE + store.
+    void* qkv = ws + wide_qkv_offset(p);
+    ColScratch sc = col_scratch(ws, col_workspace_bytes(p));
+    int* bad = reinterpret_cast<int*>(ws + kWsIndexErrorOffset);
+    if (dtype == PGB_BF16) {
+      using B = __nv_bfloat16;
+      rc = dispatch_col<B>(p, dev, x, w, T, N, K, sc, s, EpiPlain<B>{static_cast<B*>(qkv), static_cast<const B*>(bias)});
+      if (rc) return rc;
+      return launch_rope_store<B>(static_cast<const B*>(qkv), T,
+                                  make_rs<B>(q_out, k_cache, v_cache, positions, out_loc, cos_sin_cache, cache_rows,
+                                             max_position, idx64, nq, nkv, hd, rd, bad),
+                                  s);
+    }
+    using F = __half;
+    rc = dispatch_col<F>(p, dev, x, w, T, N, K, sc, s, EpiPlain<F>{static_cast<F*>(qkv), static_cast<const F*>(bias)});
+    if (rc) return rc;
+    return launch_rope_store<F>(static_cast<const F*>(qkv), T,
+                                make_rs<F>(q_out, k_cache, v_cache, positions, out_loc, cos_sin_cache, cache_rows,
+                                           max_position, idx64, nq, nkv, hd, rd, bad),
+                                s);
+  }
   if (dtype == PGB_BF16) {
     using B = __nv_bfloat16;
     const EpiRope<B> epi{make_rs<B>(q_out, k_cache, v_cache, positions, out_loc, cos_sin_cache, cache_rows,

@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
   const CommDev& cm = a.cm;
 
   if (threadIdx.x == 0) {
+    trace(1000);
     tma_prefetch_desc(&tm_a);
     tma_prefetch_desc(&tm_b);
     mbar_init(&s_epoch_bar, 1);
@@ -219,6 +220,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
     const uint32_t tmem = *c.tmem_base;
     const int row = epi_row();
     const int etid = epi_tid();
+    if (etid == 0) trace(1001);
     const IO* bias = static_cast<const IO*>(a.bias);
     int acc = 0, done = 0;
     uint32_t acc_phase = 0;
@@ -231,6 +233,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
         break;
       }
       tc_fence_after();
+      if (etid == 0 && done == 0) trace(1002);
       const int nb = tc.p * kTileP + row;
       const float b = (bias != nullptr && nb < g.N) ? io_to_f32<IO>(bias[nb]) : 0.f;
       auto emit = [&](int t, int n0, uint4 piece) { xchg_emit<IO>(a, parity, t, n0, piece); };
@@ -256,7 +259,9 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
       }
       ++done;
       named_bar_sync(1, kEpiThreads);  // every thread's stores of this piece issued
+      if (etid == 0 && done == 1) trace(1003);
       if (etid == 0) xchg_publish(cm, true, cm.rank, e, done);
+      if (etid == 0 && done == 1) trace(1004);
     }
   }
 
@@ -300,6 +305,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
       }
       ok = __syncthreads_and(wok) != 0;
       if (!ok) break;
+      if (threadIdx.x == 0 && k == 1) trace(1005);
       int t0, t1;
       piece_tokens(g, sg, BN, t0, t1);
       const int items = (t1 - t0) * per_tok;
@@ -327,6 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
       }
       __syncthreads();
       if (threadIdx.x == 0) xchg_publish(cm, false, cm.rank, e, k);
+      if (threadIdx.x == 0 && k == 1) trace(1006);
     }
   }
 
@@ -354,6 +361,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
                         ? 1
                         : 0;
     ok = __syncthreads_and(wok) != 0;
+    if (threadIdx.x == 0) trace(1007);
     if (ok) {
       const IO* base = a.oneshot ? reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes)
                                  : reinterpret_cast<const IO*>(cm.results[cm.rank] + parity * cm.result_parity_bytes);
@@ -378,7 +386,9 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
       }
     }
   }
+  if (threadIdx.x == 0) trace(1008);
   comm_end(cm, e);
+  if (threadIdx.x == 0) trace(1009);
 }
 
 template <typename IO, int BN>
@@ -481,3 +491,11 @@ int row_xchg(pgb_comm* comm, const void* x_local, const void* w_local, const voi
 }
 
 }  // namespace pgb
+
+#ifdef PGB_TRACE
+// Work builds only: point this translation unit's trace buffer at `buf`.
+extern "C" PGB_API int pgb_debug_set_trace_xchg(void* buf) {
+  cudaError_t e = cudaMemcpyToSymbol(pgb::pgb_trace_buf, &buf, sizeof(buf));
+  return e == cudaSuccess ? 0 : 2;
+}
+#endif

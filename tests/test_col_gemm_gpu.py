@@ -48,6 +48,13 @@ SHAPES = [
     (257, 512, 512),
     (1000, 1024, 1000),
     (2048, 6144, 4096),
+    # config 3 prefill (8192 tokens): qkv_proj and gate_up_proj at TP=1
+    (8192, 6144, 4096),
+    (8192, 24576, 4096),
+    # config 4 (hidden 5120) shards at TP=8: qkv 10240/8, gate_up 51200/8; T=64 and 4096
+    (64, 1280, 5120),
+    (64, 6400, 5120),
+    (4096, 6400, 5120),
 ]
 
 

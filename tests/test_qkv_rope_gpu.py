@@ -103,6 +103,10 @@ ORACLE_CASES = [
     (256, 384, 8, 1, 128, 128, False, torch.int64),
     (300, 256, 4, 2, 64, 64, True, torch.int32),
     (520, 512, 8, 2, 128, 128, False, torch.int32),
+    # head_dim 256 and 512 (rotary.py:49 accepts them): GEMM, then the standalone rotation
+    (5, 512, 4, 1, 256, 256, True, torch.int32),
+    (64, 256, 2, 1, 256, 128, False, torch.int64),
+    (300, 512, 2, 1, 512, 512, False, torch.int32),
 ]
 
 

@@ -88,6 +88,14 @@ SHAPES = [
     (3, 200, 136),
     (1000, 4096, 512),
     (2048, 4096, 4096),
+    # config 3 (prefill, 8 sequences x 1024 tokens): o_proj and down_proj at TP=1
+    (8192, 4096, 4096),
+    (8192, 4096, 12288),
+    # config 4 (hidden 5120) shards at TP=8: o_proj K = 8192/8, down_proj K = 25600/8,
+    # decode T=64 and prefill T=4096
+    (64, 5120, 3200),
+    (4096, 5120, 1024),
+    (4096, 5120, 3200),
 ]
 
 
@@ -213,3 +221,41 @@ def test_standalone_norms(pgb, cuda_device):
         ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + EPS) * wn.float()).to(dtype)
         torch.cuda.synchronize()
         assert within(o, ref, tol)[0]
+
+
+def test_f32_check_mode_matches_reference_fixture(pgb, cuda_device):
+    """BASELINE config 1 recorded from the reference itself (tests/golden/cfg1.npz,
+    made by tests/golden/make_golden.py): its LinearRowParallel at world_size 2
+    over gloo, f32, on inputs from torch.manual_seed(0) in the order x, W,
+    residual. This library's f32 check mode (one rank, full K) must give the
+    reference's all-reduced y and its residual-added sum within 1e-5 relative,
+    and the RMSNorm of that sum (restated, FlashInfer's algorithm) likewise."""
+    import importlib
+    from pathlib import Path
+
+    import numpy as np
+
+    dist = importlib.import_module("pico-sglang_b200.distributed")
+    fx = np.load(Path(__file__).resolve().parent / "golden" / "cfg1.npz")
+    torch.manual_seed(0)
+    x = torch.randn(64, 4096)
+    w = torch.randn(4096, 4096) * 0.02
+    res = torch.randn(64, 4096)
+    x, w, res = (t.to(cuda_device) for t in (x, w, res))
+    nw = torch.ones(4096, device=cuda_device)
+    comm = dist.PGBCommunicator(0, 1, 64 << 20, dist.create_uid())
+    try:
+        y = pgb.ops.row_gemm_allreduce_addnorm(comm, x, w, None, None, EPS)
+        rr = res.clone()
+        out = pgb.ops.row_gemm_allreduce_addnorm(comm, x, w, rr, nw, EPS)
+        comm.check_status()
+    finally:
+        comm.close()
+
+    def rel(a, ref):
+        ref = torch.from_numpy(ref).double()
+        return ((a.double().cpu() - ref).abs().max() / ref.pow(2).mean().sqrt()).item()
+
+    assert rel(y, fx["y"]) <= 1e-5, rel(y, fx["y"])
+    assert rel(rr, fx["residual_out"]) <= 1e-5, rel(rr, fx["residual_out"])
+    assert rel(out, fx["out_restated"]) <= 1e-5, rel(out, fx["out_restated"])
