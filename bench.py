@@ -26,7 +26,9 @@ down_proj shapes of config 2 at T = 1 and 256, and of config 4 at T = 64) at
 TP = N through the public API and compares it with the full-width f32
 restatement of the reference sequence (per-rank bf16 partials, their sum
 rounded to bf16, residual add, RMSNorm): every element within
-max(2e-2 * RMS, 2 bf16 ulp), and every rank holding bit-identical results.
+max(2e-2 * RMS, 2 bf16 ulp + the effect of one bf16 rounding flip of each
+rank's partial and of the reduced sum), and every rank holding bit-identical
+results.
 A failed check makes the process exit 1 after printing the line.
 
 Beside the headline, the same run records (all per layer, CUDA events on the
@@ -371,13 +373,17 @@ class Step:
 # ------------------------------------------------------------- parity -----
 
 
-def _within(a, ref, tol=2e-2, ulps=2):
-    """|a - ref| <= max(tol * RMS(ref), ulps * ulp(ref)) elementwise; returns
-    (ok, worst / bound, max|diff| / RMS)."""
+def _ulp(t):
+    return torch.exp2(torch.floor(torch.log2(t.float().abs().clamp_min(1e-30))) - 7)
+
+
+def _within(a, ref, tol=2e-2, ulps=2, extra=None):
+    """|a - ref| <= max(tol * RMS(ref), ulps * ulp(ref) + extra) elementwise;
+    returns (ok, worst / bound, max|diff| / RMS)."""
     ref = ref.float()
     rms = ref.pow(2).mean().sqrt().item()
     d = (a.float() - ref).abs()
-    u = ulps * torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(1e-30))) - 7)
+    u = ulps * _ulp(ref) + (extra if extra is not None else 0.0)
     worst = (d / torch.maximum(torch.full_like(d, tol * rms), u)).max().item()
     return worst <= 1.0, worst, d.max().item() / max(rms, 1e-30)
 
@@ -414,9 +420,15 @@ def parity_check(ctx: Ctx, pgb, comm) -> dict:
         ref_r = s.bfloat16()
         # The reference's output is materialised in bf16 (FlashInfer writes the
         # normalised row in the input dtype).
-        ref = (s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + EPS) * nw.float()).bfloat16()
-        ok_o, worst_o, d_o = _within(o, ref)
-        ok_r, worst_r, d_r = _within(rr, ref_r)
+        rcp = torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + EPS)
+        ref = (s * rcp * nw.float()).bfloat16()
+        # Two correct implementations may round each rank's bf16 partial and
+        # the bf16 sum to neighbouring values (different summation orders):
+        # allow one such flip per partial and in the sum, carried through the
+        # residual add and the norm.
+        dy = _ulp(y) + sum(_ulp(p_) for p_ in parts)
+        ok_o, worst_o, d_o = _within(o, ref, extra=rcp * nw.float().abs() * dy)
+        ok_r, worst_r, d_r = _within(rr, ref_r, extra=dy)
         same = True
         if n > 1:
             mine = torch.cat([o.reshape(-1), rr.reshape(-1)]).view(torch.uint8).cpu()
@@ -428,8 +440,9 @@ def parity_check(ctx: Ctx, pgb, comm) -> dict:
                       "worst_over_bound": round(max(worst_o, worst_r), 4),
                       "ranks_identical": same, "ok": bool(ok_o and ok_r and same)})
     ok = ctx.all_true(all(c["ok"] for c in cases))
-    return {"ok": ok, "bar": "max(2e-2 x RMS, 2 bf16 ulp) per element vs the full-width f32 restatement; "
-                              "all ranks bit-identical",
+    return {"ok": ok, "bar": "max(2e-2 x RMS, 2 bf16 ulp + one bf16 rounding flip of each rank partial and of "
+                              "the reduced sum carried through the norm) per element vs the full-width f32 "
+                              "restatement; all ranks bit-identical",
             "max_abs_diff_over_rms": max(c["max_abs_diff_over_rms"] for c in cases), "cases": cases}
 
 

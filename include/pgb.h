@@ -116,13 +116,13 @@ PGB_API int pgb_comm_set_one_rank_path(pgb_comm* comm, int fused);
 
 /* Multi-rank decode row ops (T <= 256, 16-bit types): which exchange
  * pgb_row_gemm_allreduce_addnorm uses.
- *   PGB_XCHG_AUTO     per-piece exchange kernel, one-shot or two-shot by a
- *                     cost model of the payload (the default)
- *   PGB_XCHG_ONESHOT  per-piece exchange, every rank reduces every row
- *   PGB_XCHG_TWOSHOT  per-piece exchange, reduce-scatter by feature slices
- *                     then all-gather of the reduced rows (needs 128 % world
- *                     == 0 and N % 128 == 0, else one-shot)
- *   PGB_XCHG_BARRIER  the grid-barrier kernel that also serves prefill shapes
+ *   PGB_XCHG_AUTO     the default: the grid-barrier kernel (one-shot or
+ *                     two-shot rows by a cost model), measured fastest
+ *   PGB_XCHG_ONESHOT  per-piece exchange kernel, every rank reduces every row
+ *   PGB_XCHG_TWOSHOT  per-piece exchange kernel, reduce-scatter by feature
+ *                     slices then all-gather of the reduced rows (needs
+ *                     128 % world == 0 and N % 128 == 0, else one-shot)
+ *   PGB_XCHG_BARRIER  the grid-barrier kernel (also serves prefill shapes)
  * Results are the same. Tuning and diagnostics; no reference counterpart. */
 #define PGB_XCHG_AUTO 0
 #define PGB_XCHG_ONESHOT 1

@@ -204,8 +204,8 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
         // then store into the slots of the reducing rank(s).
         const int nb = tc.p * kTileP + row;
         const float b = (bias != nullptr && nb < g.N) ? io_to_f32<IO>(bias[nb]) : 0.f;
-        split_reduce_tile<BN>(g, tc, c, tmem, acc, b, [&](const float* v, int t0, int t_lo, int t_hi) {
-          swap_epilogue_store<IO>(c.epi, v, t0, t_lo, t_hi, tc.p * kTileP, g.N, [&](int t, int n0, uint4 piece) {
+        split_reduce_tile<BN, IO>(g, tc, c, tmem, acc, b, [&](int t0, int t_lo, int t_hi) {
+          swap_readout(c.epi, t0, t_lo, t_hi, tc.p * kTileP, g.N, [&](int t, int n0, uint4 piece) {
             row_store_piece<IO>(a, parity, t, n0, piece);
           });
         });
@@ -465,8 +465,12 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
     return pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, dtype, stream);
   }
 
-  if (comm->exchange_mode != PGB_XCHG_BARRIER) {
-    // Decode shapes: the per-piece exchange kernel (row_xchg.cu).
+  if (comm->exchange_mode == PGB_XCHG_ONESHOT || comm->exchange_mode == PGB_XCHG_TWOSHOT) {
+    // Decode shapes on request: the per-piece exchange kernel (row_xchg.cu).
+    // Not the default: measured on two B200s it is slower than the barrier
+    // kernel below (o_proj T = 256: 42.9 vs 29.7 us; T = 1: 23.4 vs 18.0 us),
+    // because every CTA's system-scope fence before its flags costs 2-3 us,
+    // where the barrier kernel fences once per rank.
     const int rc = row_xchg(comm, x_local, w_local, bias, residual, norm_w, eps, out, T, N, K_local, dtype, stream);
     if (rc != PGB_ERR_UNSUPPORTED) return rc;
   }

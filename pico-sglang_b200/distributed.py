@@ -163,8 +163,9 @@ class PGBCommunicator:
         _lib.call("pgb_comm_set_one_rank_path", self._h, int(bool(fused)))
 
     def set_exchange_mode(self, mode: str) -> None:
-        """Multi-rank decode row ops: "auto" (default), "oneshot", "twoshot"
-        (per-piece exchange kernel) or "barrier" (the grid-barrier kernel)."""
+        """Multi-rank decode row ops: "auto" (the default, the grid-barrier
+        kernel), "oneshot" / "twoshot" (the per-piece exchange kernel) or
+        "barrier"."""
         codes = {"auto": _lib.PGB_XCHG_AUTO, "oneshot": _lib.PGB_XCHG_ONESHOT, "twoshot": _lib.PGB_XCHG_TWOSHOT,
                  "barrier": _lib.PGB_XCHG_BARRIER}
         if mode not in codes:

@@ -38,7 +38,21 @@ def ulp(ref: torch.Tensor) -> torch.Tensor:
     return torch.exp2(torch.floor(torch.log2(r)) - mant)
 
 
-def within(a, ref, tol=2e-2, ulps=2):
+def flip_allowance(x, w, residual, norm_w, eps=EPS):
+    """Per-element effect of one bf16 rounding flip of the GEMM output y.
+
+    Two correct GEMMs that sum in different orders can round a y value to
+    neighbouring bf16 numbers; the residual then moves by ulp(y) and the
+    normalised output by rsqrt(mean(s^2) + eps) * |norm_w| * ulp(y). Returns
+    (allowance for out, allowance for residual)."""
+    y = (x.float() @ w.float().t()).to(x.dtype)
+    s = y.float() + residual.float()
+    rcp = torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps)
+    uy = ulp(y)
+    return rcp * norm_w.float().abs() * uy, uy
+
+
+def within(a, ref, tol=2e-2, ulps=2, extra=None):
     """Elementwise |a - ref| <= max(tol * RMS(ref), ulps * ulp(ref)).
 
     The north-star bar is max |diff| <= 2e-2 * RMS(ref). A single rounding
@@ -47,11 +61,15 @@ def within(a, ref, tol=2e-2, ulps=2):
     residual and the output (the GEMM output, then the sum), so the bar is
     applied with a two-ulp allowance (one ulp for a plain GEMM output);
     test_reference_path_has_the_same_ulp_flips shows the reference's own
-    library path needs the allowance against an f32 restatement.
+    library path needs the allowance against an f32 restatement. `extra`
+    adds a per-element allowance (flip_allowance: one rounding flip of the
+    GEMM output carried through the norm), which matters at prefill sizes
+    where some of the 33 M outputs land on such a flip.
     """
     rms = ref.float().pow(2).mean().sqrt().item()
     d = (a.float() - ref.float()).abs()
-    bound = torch.maximum(torch.full_like(d, tol * rms), ulps * ulp(ref))
+    allow = ulps * ulp(ref) + (extra if extra is not None else 0.0)
+    bound = torch.maximum(torch.full_like(d, tol * rms), allow)
     worst = (d / bound).max().item()
     return worst <= 1.0, f"max|diff|={d.max().item():.4g} rms={rms:.4g} worst/bound={worst:.3g}"
 
@@ -107,9 +125,10 @@ def test_row_fused_addnorm_tp1(pgb, comm1, cuda_device, T, H, K):
     r_mine = r.clone()
     out = ops.row_gemm_allreduce_addnorm(comm1, x, w, r_mine, nw, EPS)
     comm1.check_status()
-    ok, msg = within(out, ref_out)
+    a_out, a_r = flip_allowance(x, w, r, nw)
+    ok, msg = within(out, ref_out, extra=a_out)
     assert ok, "out " + msg
-    ok, msg = within(r_mine, ref_r)
+    ok, msg = within(r_mine, ref_r, extra=a_r)
     assert ok, "residual " + msg
 
 
