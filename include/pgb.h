@@ -276,7 +276,9 @@ PGB_API int pgb_rope_store(const void* qkv, int T, int num_q_heads, int num_kv_h
  * which is LinearRowParallel.forward alone. out may alias nothing else.
  * On a one-rank communicator this is the column GEMM into out followed by
  * pgb_fused_add_rmsnorm (see pgb_comm_set_one_rank_path).
- * Returns PGB_ERR_INVALID for shapes the communicator's buffer cannot hold. */
+ * Payloads the communicator's buffer cannot hold run as the column GEMM into
+ * out, the chunked pgb_all_reduce, then pgb_fused_add_rmsnorm (the reference
+ * reduces them in place, csrc/src/pynccl.cu:127-135). */
 PGB_API int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_local, const void* w_local,
                                    const void* bias, void* residual, const void* norm_w,
                                    float eps, void* out, int T, int N, int K_local, int dtype,

@@ -22,9 +22,6 @@
 //   void swap_chunk(g, c, v, p, t0, t_lo, t_hi)
 //                                     swap orientation: v[j] is tile row `row`
 //                                     of token t0 + j; store tokens [t_lo, t_hi)
-//   void swap_readout_staged(g, c, p, t0, t_lo, t_hi)
-//                                     the same for a chunk already staged in
-//                                     c.epi as [32 tokens][128 rows] (split tiles)
 //   template <int BN> void nonswap_tile(g, tmem, acc, p, q)
 //                                     prefill orientation: the whole tile
 #pragma once
@@ -48,19 +45,14 @@ struct EpiPlain {
     const int n = swap_weight_row<false>(g, p, row);
     return (bias != nullptr && n >= 0) ? io_to_f32<IO>(bias[n]) : 0.f;
   }
-  // Swap orientation, chunk already staged in c.epi as [32 tokens][128 rows].
-  __device__ __forceinline__ void swap_readout_staged(const GemmShape& g, const GemmCtl& c, int p, int t0, int t_lo,
-                                                      int t_hi) const {
+  __device__ __forceinline__ void swap_chunk(const GemmShape& g, const GemmCtl& c, const float* v, int p, int t0,
+                                             int t_lo, int t_hi) const {
     IO* out = y;
     const int N = g.N;
+    swap_stage<IO>(c.epi, v);
     swap_readout(c.epi, t0, t_lo, t_hi, p * kTileP, N, [&](int t, int n0, uint4 piece) {
       *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * N + n0) = piece;
     });
-  }
-  __device__ __forceinline__ void swap_chunk(const GemmShape& g, const GemmCtl& c, const float* v, int p, int t0,
-                                             int t_lo, int t_hi) const {
-    swap_stage<IO>(c.epi, v);
-    swap_readout_staged(g, c, p, t0, t_lo, t_hi);
   }
   // Lane = token t, columns = output features.
   template <int BN>
@@ -104,18 +96,14 @@ struct EpiGlu {
     const int n = swap_weight_row<true>(g, p, row);
     return (bias != nullptr && n >= 0) ? io_to_f32<IO>(bias[n]) : 0.f;
   }
-  __device__ __forceinline__ void swap_readout_staged(const GemmShape& g, const GemmCtl& c, int p, int t0, int t_lo,
-                                                      int t_hi) const {
+  __device__ __forceinline__ void swap_chunk(const GemmShape& g, const GemmCtl& c, const float* v, int p, int t0,
+                                             int t_lo, int t_hi) const {
     IO* out = y;
     const int N = g.N;
+    swap_stage<IO>(c.epi, v);
     swap_readout_glu<IO>(c.epi, t0, t_lo, t_hi, p * (kTileP / 2), N, [&](int t, int n0, uint4 piece) {
       *reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * N + n0) = piece;
     });
-  }
-  __device__ __forceinline__ void swap_chunk(const GemmShape& g, const GemmCtl& c, const float* v, int p, int t0,
-                                             int t_lo, int t_hi) const {
-    swap_stage<IO>(c.epi, v);
-    swap_readout_staged(g, c, p, t0, t_lo, t_hi);
   }
   // Lane = token t; columns [0, BN/2) are the gate and [BN/2, BN) the up
   // values of output features q * BN/2 ... Each is rounded to IO (the
@@ -219,9 +207,10 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
       tc_fence_after();
       if (tc.nctb > 1) {
         // Split tile: reduce-scatter with the tile's other CTAs through L2.
-        split_reduce_tile<BN, IO>(g, tc, c, tmem, acc, epi.row_bias(g, tc.p, row), [&](int t0, int t_lo, int t_hi) {
-          epi.swap_readout_staged(g, c, tc.p, t0, t_lo, t_hi);
-        });
+        split_reduce_tile<BN>(g, tc, c, tmem, acc, epi.row_bias(g, tc.p, row),
+                              [&](const float* v, int t0, int t_lo, int t_hi) {
+                                epi.swap_chunk(g, c, v, tc.p, t0, t_lo, t_hi);
+                              });
       } else if constexpr (SWAP) {
         // Lane = tile row (output feature), columns = tokens.
         const float b = epi.row_bias(g, tc.p, row);

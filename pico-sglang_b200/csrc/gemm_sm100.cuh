@@ -131,19 +131,10 @@ __host__ __device__ __forceinline__ void split_cols(int V, int S, int r, int& c0
   c1 = c1 < V ? c1 : V;
 }
 
-// One [32 columns][128 rows] f32 staging buffer of the split exchange.
-constexpr int kSplitStageFloats = 32 * 128;
-
 // Bytes of a split CTA's gather area in its ring: S slots (its own and the
 // others' pieces) of its largest column run, 128 f32 per column.
-__host__ __device__ constexpr size_t split_gather_bytes(int BN, int S) {
-  return static_cast<size_t>(S) * static_cast<size_t>((BN / 4 + S - 1) / S) * 4u * 128u * 4u;
-}
-
-// Bytes a split CTA uses in its ring: the gather area, two staging buffers
-// for its outgoing partial and the 128 row biases.
 __host__ __device__ constexpr size_t split_recv_bytes(int BN, int S) {
-  return split_gather_bytes(BN, S) + 2u * kSplitStageFloats * 4u + 128u * 4u;
+  return static_cast<size_t>(S) * static_cast<size_t>((BN / 4 + S - 1) / S) * 4u * 128u * 4u;
 }
 
 // Weight tile of segment s, k-block kb, into dst (the A operand in the swap
@@ -535,7 +526,7 @@ template <typename Emit>
 __device__ __forceinline__ void swap_readout(const uint16_t* epi, int t0, int t_lo, int t_hi, int n_base, int N,
                                              Emit&& emit) {
   const int tid = epi_tid();
-#pragma unroll 1
+#pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int idx = tid + k * kEpiThreads;  // 512 pieces: 32 tokens x 16 pieces
     const int j = idx >> 4, piece = idx & 15;
@@ -551,7 +542,7 @@ template <typename IO, typename Emit>
 __device__ __forceinline__ void swap_readout_glu(const uint16_t* epi, int t0, int t_lo, int t_hi, int n_base, int N,
                                                  Emit&& emit) {
   const int tid = epi_tid();
-#pragma unroll 1
+#pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int idx = tid + k * kEpiThreads;  // 256 pieces: 32 tokens x 8 pieces
     const int j = idx >> 3, piece = idx & 7;
@@ -575,34 +566,26 @@ __device__ __forceinline__ void swap_epilogue_store(uint16_t* epi, const float* 
 // of the tile's nsplit CTAs with its partial accumulator `acc` over its own
 // k-range. The tile's real token columns are cut into nsplit runs
 // (split_cols), one per CTA. Each CTA
-//   1. moves its partial out of TMEM 32 columns at a time through a
-//      [32 columns][128 rows] f32 staging buffer in its ring (idle after its
-//      last MMA; two buffers, the next chunk's TMEM load in flight while the
-//      current one leaves), then as 16-byte pieces: the other CTAs' columns
-//      to its slab of the exchange area (token-major f32, a warp stores the
-//      512 contiguous bytes of one column), its own columns to slot j of its
-//      gather area; publishes with one release on the tile's counter;
+//   1. stores its partial for the columns the other CTAs own into its slab of
+//      the exchange area (token-major f32: a warp writes 128 contiguous bytes
+//      per token) and publishes it with one release on the tile's counter;
 //   2. once all nsplit CTAs have published, bulk-copies (cp.async.bulk, off
-//      the load/store unit) the others' pieces of its own columns into their
-//      slots of its gather area;
-//   3. per 32-token chunk of its columns, sums the S slots in split order with
-//      16-byte loads (a thread: 4 rows of one token), adds the row biases,
-//      rounds to IO and writes the chunk into the staging tile c.epi as
-//      [32 tokens][128 rows]; then readout(t0, t_lo, t_hi) stores it (all 128
-//      threads together, as after swap_stage in the whole-tile epilogue:
-//      staging row j is token t0 + j, tokens outside [t_lo, t_hi) are not
-//      stored);
+//      the load/store unit) the others' pieces of its own columns into its
+//      pipeline ring, which is idle after its last MMA;
+//   3. sums its columns in split order (its own values were parked in its
+//      ring in step 1), adds this thread's row bias `bias_v` once and hands
+//      each 32-token chunk to store_chunk(v, t0, t_lo, t_hi) (all 128
+//      threads together, as the whole-tile epilogue does: v[j] is token
+//      t0 + j, tokens outside [t_lo, t_hi) are not stored);
 //   4. bumps the tile's second counter; the last CTA to finish resets both,
 //      so the counters are zero again for the next launch.
-// bias_v is this thread's row bias. The sums run in split order, so the
-// result does not depend on timing. Returns false (and records an error) if
-// a wait runs out.
-template <int BN, typename IO, typename Readout>
+// Returns false (and records an error) if a wait runs out.
+template <int BN, typename StoreChunk>
 __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg& sg, const GemmCtl& c, uint32_t tmem,
-                                                  int acc, float bias_v, Readout&& readout) {
+                                                  int acc, float bias_v, StoreChunk&& store_chunk) {
   const int S = sg.nctb, j = sg.contrib, u = sg.tile - g.split_first;
   const int row = epi_row();
-  const int tid = epi_tid();
+  const int tid = static_cast<int>(threadIdx.x) - (kGemmThreads - kEpiThreads);
   const int t_base = sg.q * BN;
   const int V = min(BN, g.T - t_base);
   const size_t slab = static_cast<size_t>(BN) * kTileP;
@@ -610,54 +593,26 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
   int my0, my1;
   split_cols(V, S, j, my0, my1);
   bool ok = true;
-  if (tid == 0) trace(1010);
 
-  // Ring layout: gather area [S][n_mine][128] f32, two staging buffers,
-  // 128 row biases.
+  // 1. This CTA's partial: the other CTAs' columns to its exchange slab, its
+  //    own columns to slot j of the gather area in its ring (idle after the
+  //    last MMA), laid out [S][n_mine][128] f32.
   const int n_mine = my1 - my0;
   float* recv = reinterpret_cast<float*>(c.a);
-  float* stage = recv + split_gather_bytes(BN, S) / 4;
-  float* sbias = stage + 2 * kSplitStageFloats;
   float* mine = g.xchg + static_cast<size_t>(u * S + j) * slab;
-  float* own = recv + static_cast<size_t>(j) * n_mine * kTileP;
-  sbias[row] = bias_v;
-
-  // 1. This CTA's partial out of TMEM. Buffer ci & 1 was last read for chunk
-  //    ci - 2, before every thread arrived at chunk ci - 1's barrier.
-  auto stage_out = [&](uint32_t(&r)[32], int ci) {
-    float* st = stage + (ci & 1) * kSplitStageFloats;
+  float* own = recv + static_cast<size_t>(j) * n_mine * kTileP + row;
+#pragma unroll 1
+  for (int cb = 0; cb < V; cb += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, cb), r);
+    tmem_ld_wait();
 #pragma unroll
-    for (int jj = 0; jj < 32; ++jj) st[jj * kTileP + row] = __uint_as_float(r[jj]);
-    named_bar_sync(1, kEpiThreads);
-    const int cb = ci * 32;
-    // Rolled: this tail runs once per launch with a cold instruction cache,
-    // so a short loop body fetched once beats straight-line code.
-#pragma unroll 1
-    for (int m = 0; m < 8; ++m) {
-      const int idx = tid + m * kEpiThreads;  // 32 columns x 32 quads of rows
-      const int cl = idx >> 5, r4 = (idx & 31) * 4;
-      const int col = cb + cl;
-      if (col < V) {
-        const float4 val = *reinterpret_cast<const float4*>(st + cl * kTileP + r4);
-        if (col >= my0 && col < my1)
-          *reinterpret_cast<float4*>(own + static_cast<size_t>(col - my0) * kTileP + r4) = val;
-        else
-          __stcg(reinterpret_cast<float4*>(mine + static_cast<size_t>(col) * kTileP + r4), val);
-      }
-    }
-  };
-  const int nch = (V + 31) >> 5;
-  uint32_t ra[32], rb[32];
-  if (nch > 0) tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, 0), ra);
-#pragma unroll 1
-  for (int ci = 0; ci < nch; ci += 2) {
-    tmem_ld_wait(ra);
-    if (ci + 1 < nch) tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, (ci + 1) * 32), rb);
-    stage_out(ra, ci);
-    if (ci + 1 < nch) {
-      tmem_ld_wait(rb);
-      if (ci + 2 < nch) tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, (ci + 2) * 32), ra);
-      stage_out(rb, ci + 1);
+    for (int jj = 0; jj < 32; ++jj) {
+      const int col = cb + jj;
+      const float x = __uint_as_float(r[jj]);
+      const bool is_mine = col >= my0 && col < my1;
+      if (is_mine) own[static_cast<size_t>(col - my0) * kTileP] = x;
+      if (!is_mine && col < V) __stcg(mine + static_cast<size_t>(col) * kTileP + row, x);
     }
   }
   // bar.sync, then one gpu-scope release: every thread's stores are ordered
@@ -706,40 +661,29 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
     ok = *reinterpret_cast<volatile int*>(c.flag) != 0;
   }
 
-  // 3. Sum the S slots in split order, add the bias, round, stage, store.
-  //    Token indices past this CTA's run are clamped (those rows of the
-  //    staging tile are not emitted).
+  // 3. Sum the S slots in split order, add the bias, round, store. Shared
+  //    memory only and branch-free: token indices past this CTA's run are
+  //    clamped (those lanes of the staging tile are not emitted).
   if (ok && n_mine > 0) {
-    const size_t slot_stride = static_cast<size_t>(n_mine) * kTileP;
+    const float* base = recv + row;
 #pragma unroll 1
     for (int c0 = 0; c0 < n_mine; c0 += 32) {
       if (tid == 0 && c0 == 0) trace(1014);
-      named_bar_sync(1, kEpiThreads);  // the previous readout has finished with c.epi
+      const int lim = n_mine - 1 - c0;
+      float v[32];
+      const float* s0 = base + static_cast<size_t>(c0) * kTileP;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) v[jj] = s0[static_cast<size_t>(min(jj, lim)) * kTileP];
 #pragma unroll 1
-      for (int m = 0; m < 8; ++m) {
-        const int idx = tid + m * kEpiThreads;  // 32 tokens x 32 quads of rows
-        const int jt = idx >> 5, r4 = (idx & 31) * 4;
-        const float* src = recv + static_cast<size_t>(min(c0 + jt, n_mine - 1)) * kTileP + r4;
-        float4 a = *reinterpret_cast<const float4*>(src);
-#pragma unroll 1
-        for (int q = 1; q < S; ++q) {
-          const float4 b = *reinterpret_cast<const float4*>(src + q * slot_stride);
-          a.x += b.x;
-          a.y += b.y;
-          a.z += b.z;
-          a.w += b.w;
-        }
-        const float4 bb = *reinterpret_cast<const float4*>(sbias + r4);
-        a.x += bb.x;
-        a.y += bb.y;
-        a.z += bb.z;
-        a.w += bb.w;
-        IO h[4] = {f32_to_io<IO>(a.x), f32_to_io<IO>(a.y), f32_to_io<IO>(a.z), f32_to_io<IO>(a.w)};
-        *reinterpret_cast<uint2*>(c.epi + jt * kTileP + r4) = *reinterpret_cast<const uint2*>(h);
+      for (int q = 1; q < S; ++q) {
+        const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) v[jj] += sq[static_cast<size_t>(min(jj, lim)) * kTileP];
       }
-      named_bar_sync(1, kEpiThreads);
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) v[jj] += bias_v;
       if (tid == 0 && c0 == 0) trace(1015);
-      readout(t_base + my0 + c0, t_base + my0, t_base + my1);
+      store_chunk(v, t_base + my0 + c0, t_base + my0, t_base + my1);
       if (tid == 0 && c0 == 0) trace(1016);
     }
   }

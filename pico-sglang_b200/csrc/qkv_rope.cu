@@ -167,11 +167,6 @@ struct EpiRope {
   __device__ __forceinline__ void swap_chunk(const GemmShape& g, const GemmCtl& c, const float* v, int p, int t0,
                                              int t_lo, int t_hi) const {
     swap_stage<IO>(c.epi, v);
-    swap_readout_staged(g, c, p, t0, t_lo, t_hi);
-  }
-  // The chunk is staged in c.epi as [32 tokens][128 rows].
-  __device__ __forceinline__ void swap_readout_staged(const GemmShape& g, const GemmCtl& c, int p, int t0, int t_lo,
-                                                      int t_hi) const {
     const int tid = epi_tid();
     const int jb = tid >> 4, row0 = (tid & 15) * 8;
     const int f0 = p * kTileP + row0;

@@ -204,8 +204,8 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
         // then store into the slots of the reducing rank(s).
         const int nb = tc.p * kTileP + row;
         const float b = (bias != nullptr && nb < g.N) ? io_to_f32<IO>(bias[nb]) : 0.f;
-        split_reduce_tile<BN, IO>(g, tc, c, tmem, acc, b, [&](int t0, int t_lo, int t_hi) {
-          swap_readout(c.epi, t0, t_lo, t_hi, tc.p * kTileP, g.N, [&](int t, int n0, uint4 piece) {
+        split_reduce_tile<BN>(g, tc, c, tmem, acc, b, [&](const float* v, int t0, int t_lo, int t_hi) {
+          swap_epilogue_store<IO>(c.epi, v, t0, t_lo, t_hi, tc.p * kTileP, g.N, [&](int t, int n0, uint4 piece) {
             row_store_piece<IO>(a, parity, t, n0, piece);
           });
         });

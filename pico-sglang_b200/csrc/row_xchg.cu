@@ -238,8 +238,8 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
       const float b = (bias != nullptr && nb < g.N) ? io_to_f32<IO>(bias[nb]) : 0.f;
       auto emit = [&](int t, int n0, uint4 piece) { xchg_emit<IO>(a, parity, t, n0, piece); };
       if (tc.nctb > 1) {
-        split_reduce_tile<BN, IO>(g, tc, c, tmem, acc, b, [&](int t0, int t_lo, int t_hi) {
-          swap_readout(c.epi, t0, t_lo, t_hi, tc.p * kTileP, g.N, emit);
+        split_reduce_tile<BN>(g, tc, c, tmem, acc, b, [&](const float* v, int t0, int t_lo, int t_hi) {
+          swap_epilogue_store<IO>(c.epi, v, t0, t_lo, t_hi, tc.p * kTileP, g.N, emit);
         });
       } else {
 #pragma unroll 1
