@@ -123,12 +123,37 @@ PGB_API int pgb_comm_set_one_rank_path(pgb_comm* comm, int fused);
  *                     slices then all-gather of the reduced rows (needs
  *                     128 % world == 0 and N % 128 == 0, else one-shot)
  *   PGB_XCHG_BARRIER  the grid-barrier kernel (also serves prefill shapes)
- * Results are the same. Tuning and diagnostics; no reference counterpart. */
+ *   PGB_XCHG_NVLS     partials stay in this GPU's multicast-bound memory; the
+ *                     owner of each slice sums it over every GPU with
+ *                     multimem.ld_reduce and broadcasts it with multimem.st
+ * Results are the same within the bf16 bar (NVLS sums in the switch with f32
+ * accumulation). Tuning and diagnostics; no reference counterpart. */
 #define PGB_XCHG_AUTO 0
 #define PGB_XCHG_ONESHOT 1
 #define PGB_XCHG_TWOSHOT 2
 #define PGB_XCHG_BARRIER 3
+#define PGB_XCHG_NVLS 4  /* NVLink multicast reduce (needs pgb_comm_nvls_bind; else auto) */
 PGB_API int pgb_comm_set_exchange_mode(pgb_comm* comm, int mode);
+
+/* NVLink multicast (NVLS) for the row op's reduction, set up after
+ * pgb_comm_open_peers; no reference counterpart (the reference's NCCL may use
+ * NVLS inside ncclAllReduce, csrc/src/pynccl.cu:84-92,127). Sequence, each
+ * step on every rank before any rank starts the next (a host barrier):
+ *   1. rank 0: pgb_comm_nvls_create(comm, &fd) creates the multicast object
+ *      of the team and exports it as a POSIX file descriptor, which the host
+ *      passes to the other ranks' processes (e.g. SCM_RIGHTS over a Unix
+ *      socket);
+ *   2. every rank: pgb_comm_nvls_add(comm, fd) imports it (ranks != 0; the
+ *      caller closes its fd afterwards) and adds this device to the team;
+ *   3. every rank: pgb_comm_nvls_bind(comm) binds and maps this device's
+ *      memory (2 x 2 x max_bytes, rounded to the multicast granularity).
+ * pgb_comm_nvls_supported reports whether the device can take part.
+ * pgb_comm_destroy releases everything; call it on every rank after the last
+ * kernel, never while another rank may still be inside a call. */
+PGB_API int pgb_comm_nvls_supported(pgb_comm* comm, int* out);
+PGB_API int pgb_comm_nvls_create(pgb_comm* comm, int* fd_out);
+PGB_API int pgb_comm_nvls_add(pgb_comm* comm, int fd);
+PGB_API int pgb_comm_nvls_bind(pgb_comm* comm);
 
 /* Read the device status word (0 = ok, else PGB_ERR_TIMEOUT etc. as the
  * device recorded it); reset it to 0 when reset != 0. Synchronises the

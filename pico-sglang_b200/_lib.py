@@ -31,6 +31,7 @@ PGB_XCHG_AUTO = 0
 PGB_XCHG_ONESHOT = 1
 PGB_XCHG_TWOSHOT = 2
 PGB_XCHG_BARRIER = 3
+PGB_XCHG_NVLS = 4
 UID_BYTES = 128
 MAX_RANKS = 8
 
@@ -69,6 +70,10 @@ _SIGS: dict[str, tuple[object, list[object]]] = {
     "pgb_comm_get_status": (c_int, [c_void_p, POINTER(c_int), c_int]),
     "pgb_comm_set_one_rank_path": (c_int, [c_void_p, c_int]),
     "pgb_comm_set_exchange_mode": (c_int, [c_void_p, c_int]),
+    "pgb_comm_nvls_supported": (c_int, [c_void_p, POINTER(c_int)]),
+    "pgb_comm_nvls_create": (c_int, [c_void_p, POINTER(c_int)]),
+    "pgb_comm_nvls_add": (c_int, [c_void_p, c_int]),
+    "pgb_comm_nvls_bind": (c_int, [c_void_p]),
     "pgb_comm_get_buffer": (c_int, [c_void_p, POINTER(c_void_p)]),
     "pgb_all_reduce": (c_int, [c_void_p, c_void_p, c_size_t, c_int, c_int, c_void_p]),
     "pgb_all_gather": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_int, c_void_p]),

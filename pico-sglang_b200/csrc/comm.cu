@@ -11,6 +11,8 @@
 
 #include <chrono>
 #include <cstring>
+#include <algorithm>
+#include <mutex>
 #include <new>
 
 #include "comm.h"
@@ -377,10 +379,248 @@ extern "C" int pgb_comm_open_peers(pgb_comm* comm, const uint8_t* handles) {
   return PGB_OK;
 }
 
+// ------------------------------------------------------------------ NVLS --
+// NVLink multicast objects through the driver API, resolved at run time
+// (cudaGetDriverEntryPoint), so the library does not link libcuda.
+
+namespace pgb {
+namespace {
+
+struct NvlsDriver {
+  decltype(&cuMulticastCreate) mc_create = nullptr;
+  decltype(&cuMulticastAddDevice) mc_add = nullptr;
+  decltype(&cuMulticastBindMem) mc_bind = nullptr;
+  decltype(&cuMulticastUnbind) mc_unbind = nullptr;
+  decltype(&cuMulticastGetGranularity) mc_gran = nullptr;
+  decltype(&cuMemCreate) mem_create = nullptr;
+  decltype(&cuMemRelease) mem_release = nullptr;
+  decltype(&cuMemExportToShareableHandle) mem_export = nullptr;
+  decltype(&cuMemImportFromShareableHandle) mem_import = nullptr;
+  decltype(&cuMemAddressReserve) va_reserve = nullptr;
+  decltype(&cuMemAddressFree) va_free = nullptr;
+  decltype(&cuMemMap) mem_map = nullptr;
+  decltype(&cuMemUnmap) mem_unmap = nullptr;
+  decltype(&cuMemSetAccess) mem_access = nullptr;
+  decltype(&cuMemGetAllocationGranularity) mem_gran = nullptr;
+  decltype(&cuDeviceGetAttribute) dev_attr = nullptr;
+  bool ok = false;
+};
+
+template <typename F>
+bool resolve(const char* name, F& out) {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &fn, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess ||
+      fn == nullptr)
+    return false;
+  out = reinterpret_cast<F>(fn);
+  return true;
+}
+
+const NvlsDriver& nvls_driver() {
+  static NvlsDriver d;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    d.ok = resolve("cuMulticastCreate", d.mc_create) && resolve("cuMulticastAddDevice", d.mc_add) &&
+           resolve("cuMulticastBindMem", d.mc_bind) && resolve("cuMulticastUnbind", d.mc_unbind) &&
+           resolve("cuMulticastGetGranularity", d.mc_gran) && resolve("cuMemCreate", d.mem_create) &&
+           resolve("cuMemRelease", d.mem_release) && resolve("cuMemExportToShareableHandle", d.mem_export) &&
+           resolve("cuMemImportFromShareableHandle", d.mem_import) && resolve("cuMemAddressReserve", d.va_reserve) &&
+           resolve("cuMemAddressFree", d.va_free) && resolve("cuMemMap", d.mem_map) &&
+           resolve("cuMemUnmap", d.mem_unmap) && resolve("cuMemSetAccess", d.mem_access) &&
+           resolve("cuMemGetAllocationGranularity", d.mem_gran) && resolve("cuDeviceGetAttribute", d.dev_attr);
+  });
+  return d;
+}
+
+int cu_error(CUresult r, const char* what) {
+  return set_error(PGB_ERR_CUDA, "%s failed (CUresult %d)", what, static_cast<int>(r));
+}
+
+#define PGB_CU_TRY(expr)                                  \
+  do {                                                    \
+    CUresult _r = (expr);                                 \
+    if (_r != CUDA_SUCCESS) return ::pgb::cu_error(_r, #expr); \
+  } while (0)
+
+CUmulticastObjectProp nvls_prop(const pgb_comm* c) {
+  CUmulticastObjectProp prop{};
+  prop.numDevices = static_cast<unsigned int>(c->world);
+  prop.size = c->nv_bytes;
+  prop.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  prop.flags = 0;
+  return prop;
+}
+
+// Size of the multicast region: two parities of [partials | reduced] of
+// max_bytes each, rounded to the multicast and allocation granularities.
+int nvls_size(pgb_comm* c) {
+  const NvlsDriver& d = nvls_driver();
+  c->nv_parity_bytes = 2 * align_up(c->max_bytes, 4096);
+  CUmulticastObjectProp prop{};
+  prop.numDevices = static_cast<unsigned int>(c->world);
+  prop.size = 2 * c->nv_parity_bytes;
+  prop.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  size_t mc_gran = 0, mem_gran = 0;
+  PGB_CU_TRY(d.mc_gran(&mc_gran, &prop, CU_MULTICAST_GRANULARITY_MINIMUM));
+  CUmemAllocationProp mp{};
+  mp.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  mp.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  mp.location.id = c->device;
+  mp.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  PGB_CU_TRY(d.mem_gran(&mem_gran, &mp, CU_MEM_ALLOC_GRANULARITY_MINIMUM));
+  const size_t gran = std::max(mc_gran, mem_gran);
+  c->nv_bytes = align_up(2 * c->nv_parity_bytes, gran);
+  return PGB_OK;
+}
+
+void nvls_release(pgb_comm* c) {
+  const NvlsDriver& d = nvls_driver();
+  if (!d.ok) return;
+  CUdevice dev = c->device;
+  if (c->nv_mc != 0) {
+    d.mem_unmap(c->nv_mc, c->nv_bytes);
+    d.va_free(c->nv_mc, c->nv_bytes);
+    c->nv_mc = 0;
+  }
+  if (c->nv_bound) {
+    d.mc_unbind(static_cast<CUmemGenericAllocationHandle>(c->nv_mc_handle), dev, 0, c->nv_bytes);
+    c->nv_bound = false;
+  }
+  if (c->nv_uc != 0) {
+    d.mem_unmap(c->nv_uc, c->nv_bytes);
+    d.va_free(c->nv_uc, c->nv_bytes);
+    c->nv_uc = 0;
+  }
+  if (c->nv_mem_handle != 0) {
+    d.mem_release(static_cast<CUmemGenericAllocationHandle>(c->nv_mem_handle));
+    c->nv_mem_handle = 0;
+  }
+  if (c->nv_mc_handle != 0) {
+    d.mem_release(static_cast<CUmemGenericAllocationHandle>(c->nv_mc_handle));
+    c->nv_mc_handle = 0;
+  }
+  c->nvls = false;
+  c->nv_added = false;
+}
+
+}  // namespace
+}  // namespace pgb
+
+extern "C" int pgb_comm_nvls_supported(pgb_comm* comm, int* out) {
+  if (comm == nullptr || out == nullptr) return set_error(PGB_ERR_INVALID, "nvls_supported: null argument");
+  *out = 0;
+  const NvlsDriver& d = nvls_driver();
+  if (!d.ok || comm->world < 2) return PGB_OK;
+  int v = 0;
+  if (d.dev_attr(&v, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, comm->device) == CUDA_SUCCESS) *out = v != 0;
+  return PGB_OK;
+}
+
+extern "C" int pgb_comm_nvls_create(pgb_comm* comm, int* fd_out) {
+  if (comm == nullptr || fd_out == nullptr) return set_error(PGB_ERR_INVALID, "nvls_create: null argument");
+  if (comm->rank != 0) return set_error(PGB_ERR_INVALID, "nvls_create: rank 0 creates the multicast object");
+  if (comm->nv_mc_handle != 0) return set_error(PGB_ERR_STATE, "nvls_create: already created");
+  const NvlsDriver& d = nvls_driver();
+  if (!d.ok) return set_error(PGB_ERR_UNSUPPORTED, "nvls_create: multicast driver API unavailable");
+  DeviceGuard g(comm->device);
+  int rc = nvls_size(comm);
+  if (rc) return rc;
+  CUmulticastObjectProp prop = nvls_prop(comm);
+  CUmemGenericAllocationHandle h = 0;
+  PGB_CU_TRY(d.mc_create(&h, &prop));
+  comm->nv_mc_handle = h;
+  int fd = -1;
+  const CUresult r = d.mem_export(&fd, h, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0);
+  if (r != CUDA_SUCCESS) {
+    nvls_release(comm);
+    return cu_error(r, "cuMemExportToShareableHandle(multicast)");
+  }
+  *fd_out = fd;
+  return PGB_OK;
+}
+
+extern "C" int pgb_comm_nvls_add(pgb_comm* comm, int fd) {
+  if (comm == nullptr) return set_error(PGB_ERR_INVALID, "nvls_add: null communicator");
+  if (comm->world > 1 && !comm->peers_open) return set_error(PGB_ERR_STATE, "nvls_add: peers not opened");
+  const NvlsDriver& d = nvls_driver();
+  if (!d.ok) return set_error(PGB_ERR_UNSUPPORTED, "nvls_add: multicast driver API unavailable");
+  DeviceGuard g(comm->device);
+  if (comm->rank != 0) {
+    if (comm->nv_mc_handle != 0) return set_error(PGB_ERR_STATE, "nvls_add: already added");
+    if (fd < 0) return set_error(PGB_ERR_INVALID, "nvls_add: no file descriptor");
+    int rc = nvls_size(comm);
+    if (rc) return rc;
+    CUmemGenericAllocationHandle h = 0;
+    PGB_CU_TRY(d.mem_import(&h, reinterpret_cast<void*>(static_cast<uintptr_t>(fd)),
+                            CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR));
+    comm->nv_mc_handle = h;
+  } else if (comm->nv_mc_handle == 0) {
+    return set_error(PGB_ERR_STATE, "nvls_add: rank 0 has not created the multicast object");
+  }
+  const CUresult r = d.mc_add(static_cast<CUmemGenericAllocationHandle>(comm->nv_mc_handle), comm->device);
+  if (r != CUDA_SUCCESS) return cu_error(r, "cuMulticastAddDevice");
+  comm->nv_added = true;
+  return PGB_OK;
+}
+
+extern "C" int pgb_comm_nvls_bind(pgb_comm* comm) {
+  if (comm == nullptr) return set_error(PGB_ERR_INVALID, "nvls_bind: null communicator");
+  if (!comm->nv_added) return set_error(PGB_ERR_STATE, "nvls_bind: device not added (pgb_comm_nvls_add)");
+  if (comm->nv_bound) return PGB_OK;
+  const NvlsDriver& d = nvls_driver();
+  DeviceGuard g(comm->device);
+  const CUmemGenericAllocationHandle mc = static_cast<CUmemGenericAllocationHandle>(comm->nv_mc_handle);
+  CUmemAllocationProp mp{};
+  mp.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+  mp.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  mp.location.id = comm->device;
+  mp.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+  CUmemGenericAllocationHandle mem = 0;
+  PGB_CU_TRY(d.mem_create(&mem, comm->nv_bytes, &mp, 0));
+  comm->nv_mem_handle = mem;
+  CUmemAccessDesc acc{};
+  acc.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+  acc.location.id = comm->device;
+  acc.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+  CUdeviceptr uc = 0, mcp = 0;
+  int rc = PGB_OK;
+  CUresult r = d.va_reserve(&uc, comm->nv_bytes, 0, 0, 0);
+  if (r == CUDA_SUCCESS) {
+    comm->nv_uc = uc;  // released by nvls_release even if the map below fails
+    r = d.mem_map(uc, comm->nv_bytes, 0, mem, 0);
+    if (r == CUDA_SUCCESS) r = d.mem_access(uc, comm->nv_bytes, &acc, 1);
+  }
+  if (r == CUDA_SUCCESS) {
+    r = d.mc_bind(mc, 0, mem, 0, comm->nv_bytes, 0);
+    if (r == CUDA_SUCCESS) comm->nv_bound = true;
+  }
+  if (r == CUDA_SUCCESS) {
+    r = d.va_reserve(&mcp, comm->nv_bytes, 0, 0, 0);
+    if (r == CUDA_SUCCESS) {
+      comm->nv_mc = mcp;
+      r = d.mem_map(mcp, comm->nv_bytes, 0, mc, 0);
+      if (r == CUDA_SUCCESS) r = d.mem_access(mcp, comm->nv_bytes, &acc, 1);
+    }
+  }
+  if (r == CUDA_SUCCESS) {
+    const cudaError_t e = cudaMemset(reinterpret_cast<void*>(uc), 0, comm->nv_bytes);
+    if (e != cudaSuccess) rc = cuda_error(e, "cudaMemset(nvls region)");
+    const cudaError_t e2 = cudaDeviceSynchronize();
+    if (!rc && e2 != cudaSuccess) rc = cuda_error(e2, "nvls_bind: synchronise");
+  } else {
+    rc = cu_error(r, "nvls_bind: map / bind");
+  }
+  if (rc) return rc;  // partial state is released by pgb_comm_destroy
+  comm->nvls = true;
+  return PGB_OK;
+}
+
 extern "C" int pgb_comm_destroy(pgb_comm* comm) {
   if (comm == nullptr) return PGB_OK;
   DeviceGuard g(comm->device);
   cudaDeviceSynchronize();
+  pgb::nvls_release(comm);
   for (int r = 0; r < comm->world; ++r)
     if (r != comm->rank && comm->peer[r] != nullptr) cudaIpcCloseMemHandle(comm->peer[r]);
   cudaFree(comm->local);
@@ -404,7 +644,7 @@ extern "C" int pgb_comm_set_one_rank_path(pgb_comm* comm, int fused) {
 
 extern "C" int pgb_comm_set_exchange_mode(pgb_comm* comm, int mode) {
   if (comm == nullptr) return set_error(PGB_ERR_INVALID, "set_exchange_mode: null communicator");
-  if (mode < PGB_XCHG_AUTO || mode > PGB_XCHG_BARRIER)
+  if (mode < PGB_XCHG_AUTO || mode > PGB_XCHG_NVLS)
     return set_error(PGB_ERR_INVALID, "set_exchange_mode: unknown mode %d", mode);
   comm->exchange_mode = mode;
   return PGB_OK;

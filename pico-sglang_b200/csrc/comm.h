@@ -6,9 +6,6 @@
 //   [header 4 KB]  magic, uid, world size, layout sizes (checked by peers)
 //   [flags  4 KB]  flags[bar][src_rank]: epoch written by src when it passed
 //                  cross-rank barrier `bar`
-//   [piece flags 2 x 32 KB]  per-piece arrival flags of the exchange kernel
-//                  (row_xchg.cu): rs[src_rank][cta] and ag[owner_rank][cta],
-//                  each (epoch << 8 | pieces delivered by that CTA)
 //   [user buffer]  max_bytes, returned by get_buffer
 //   [slots  x 2]   two parities of partial rows pushed by the ranks:
 //                  slot[src_rank][row][width]
@@ -35,11 +32,8 @@ namespace pgb {
 
 constexpr int kNumBars = 4;          // flags per rank: barrier ids 0..3
 constexpr size_t kHeaderBytes = 4096;
-constexpr size_t kBarFlagBytes = 4096;
-constexpr int kXchgMaxCtas = 1024;   // piece-flag rows are this many CTAs wide
-constexpr size_t kXchgFlagBytes = static_cast<size_t>(PGB_MAX_RANKS) * kXchgMaxCtas * 4u;
-constexpr size_t kFlagBytes = kBarFlagBytes + 2 * kXchgFlagBytes;
-constexpr uint64_t kCommMagic = 0x3130324247504255ull;  // layout tag
+constexpr size_t kFlagBytes = 4096;
+constexpr uint64_t kCommMagic = 0x3230324247504255ull;  // layout tag
 constexpr size_t kSplitScratchBytes = 32u << 20;        // split-tile exchange area per comm
 constexpr size_t kTileCounterBytes = 64u << 10;
 
@@ -70,7 +64,7 @@ struct CommDev {
   int world;
   uint8_t* slots[PGB_MAX_RANKS];    // slot region base (parity 0) of each rank
   uint8_t* results[PGB_MAX_RANKS];  // result region base (parity 0) of each rank
-  uint32_t* flags[PGB_MAX_RANKS];   // flag area of each rank (barrier flags, then the piece flags)
+  uint32_t* flags[PGB_MAX_RANKS];   // flag area of each rank
   uint64_t slot_parity_bytes;
   uint64_t result_parity_bytes;
   uint32_t* epoch;
@@ -78,15 +72,6 @@ struct CommDev {
   int* status;
   uint64_t timeout_ns;
 };
-
-// Piece flags of rank `d` (see the layout above): reduce-scatter arrivals
-// rs[src][cta] and all-gather arrivals ag[owner][cta].
-__host__ __device__ inline uint32_t* xchg_rs_flags(const CommDev& cm, int d) {
-  return cm.flags[d] + kBarFlagBytes / 4;
-}
-__host__ __device__ inline uint32_t* xchg_ag_flags(const CommDev& cm, int d) {
-  return cm.flags[d] + (kBarFlagBytes + kXchgFlagBytes) / 4;
-}
 
 }  // namespace pgb
 
@@ -107,6 +92,17 @@ struct pgb_comm {
   int sm_count;
   int one_rank_fused = 0;  // world == 1: run the row op as the fused kernel (else GEMM + norm)
   int exchange_mode = PGB_XCHG_AUTO;  // multi-rank decode row ops, see pgb_comm_set_exchange_mode
+  // NVLink multicast (NVLS) region, see pgb_comm_nvls_create: one physical
+  // allocation on this device bound to a multicast object of the team,
+  // mapped twice: nv_uc reaches this device's copy, nv_mc all copies at once.
+  // Per parity: [partials max_bytes | reduced max_bytes].
+  bool nvls = false;
+  unsigned long long nv_mc_handle = 0;   // CUmemGenericAllocationHandle of the multicast object
+  unsigned long long nv_mem_handle = 0;  // CUmemGenericAllocationHandle of this device's memory
+  bool nv_added = false, nv_bound = false;
+  unsigned long long nv_uc = 0, nv_mc = 0;  // CUdeviceptr of the two views (0: not mapped)
+  size_t nv_bytes = 0;
+  size_t nv_parity_bytes = 0;
 };
 
 namespace pgb {

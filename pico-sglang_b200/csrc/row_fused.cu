@@ -465,7 +465,8 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
     return pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, dtype, stream);
   }
 
-  if (comm->exchange_mode == PGB_XCHG_ONESHOT || comm->exchange_mode == PGB_XCHG_TWOSHOT) {
+  if (comm->exchange_mode == PGB_XCHG_ONESHOT || comm->exchange_mode == PGB_XCHG_TWOSHOT ||
+      (comm->exchange_mode == PGB_XCHG_NVLS && comm->nvls)) {
     // Decode shapes on request: the per-piece exchange kernel (row_xchg.cu).
     // Not the default: measured on two B200s it is slower than the barrier
     // kernel below (o_proj T = 256: 42.9 vs 29.7 us; T = 1: 23.4 vs 18.0 us),

@@ -1,5 +1,5 @@
 // row_xchg.cu - row-parallel GEMM + all-reduce + residual-add + RMSNorm on
-// several GPUs for decode shapes, with a per-piece exchange.
+// several GPUs for decode shapes, with a feature-slice exchange.
 //
 // Replaces, per call, the reference sequence
 //   LinearRowParallel.forward   y = F.linear(x_local, W_local)         (layers/linear.py:90-97)
@@ -10,26 +10,28 @@
 //
 // Every rank runs the same work decomposition, so CTA c computes "piece" k
 // (its k-th segment: a whole tile, or its token run of a split tile) of the
-// same output region on every rank. The exchange works piece by piece,
-// synchronised by flags that carry (epoch << 8 | pieces delivered), written
-// with one system-scope fence per piece and read with acquire loads. There is
-// no grid-wide barrier.
+// same output region on every rank.
 //
-// Two-shot (reduce-scatter + all-gather of the reduced sum):
-//   1. GEMM. Each 16-byte piece of 8 output features of the finished piece
+// Two-shot (reduce-scatter by feature slices + all-gather of the reduced sum):
+//   1. GEMM. Each 16-byte piece of 8 output features of a finished piece
 //      (split tiles reduce-scattered on this GPU first, rounded to the I/O
 //      type as F.linear rounds) goes to the rank owning that feature slice:
 //      rank s owns features [s*F, (s+1)*F) of every 128-feature tile,
-//      F = 128 / world. Then flag rs[rank][c] on every rank.
-//   2. CTA c on rank s waits for rs[*][c] of every rank, sums its slice of
-//      the piece over the ranks in rank order (f32), rounds it (the reference
-//      materialises the reduced tensor), and stores it into every rank's y
-//      buffer [T][H]. Then flag ag[s][c] on every rank.
-//   3. Once every piece's slices have arrived (all ag flags), each rank
-//      computes residual += y and out = rmsnorm(residual) for all rows from
-//      its own y buffer and residual copy: every rank ends bit-identical.
-// One-shot (small T, where latency dominates): step 1 sends the whole piece
-// to every rank, step 2 is skipped, and step 3 sums the ranks' pieces itself.
+//      F = 128 / world. Barrier 0 (every CTA arrives, one system-scope fence
+//      and a flag per rank, then every CTA waits for all ranks).
+//   2. CTA c on rank s sums its slice of each of its pieces over the ranks in
+//      rank order (f32), rounds it (the reference materialises the reduced
+//      tensor), and stores it into every rank's y buffer [T][H]. Barrier 1.
+//   3. Every rank computes residual += y and out = rmsnorm(residual) for its
+//      rows from its own y buffer and its own residual copy: every rank ends
+//      bit-identical. The all-gather carries y only, half the bytes of
+//      gathering out and residual.
+// One-shot (small payloads): step 1 sends the whole piece to every rank,
+// step 2 is skipped, and step 3 sums the ranks' pieces itself.
+//
+// Each reduction step is spread over every CTA that computed a piece (the
+// slices follow the GEMM's own decomposition), where the token-row owners of
+// row_fused.cu leave most CTAs idle at small T.
 //
 // Bytes over NVLink per rank: two-shot 2 (n-1)/n T H 2 (the P2P bound),
 // one-shot (n-1) T H 2.
@@ -48,6 +50,10 @@ constexpr int kXchgRowMaxVec = 8;  // width <= 192 threads x 8 vectors x 8 eleme
 struct XchgArgs {
   GemmShape g;
   CommDev cm;
+  int nvls;      // NVLink multicast: partials local, reduced in the switch
+  uint8_t* nv_uc;  // this device's view of the multicast-bound region
+  uint8_t* nv_mc;  // the multicast view (every device of the team)
+  uint64_t nv_parity_bytes;  // per parity: [partials | reduced], half each
   int oneshot;
   int fslice;  // two-shot: features of a 128-feature tile owned by each rank (128 / world)
   void* out;
@@ -57,18 +63,6 @@ struct XchgArgs {
   float eps;
   int do_norm;
 };
-
-__host__ __device__ __forceinline__ uint32_t xchg_pack(uint32_t e, uint32_t pieces) { return (e << 8) | pieces; }
-
-// Pieces (segments) CTA c computes: its rounds of whole tiles, then its split
-// segment, as SegIter walks them.
-__host__ __device__ __forceinline__ int cta_pieces(const GemmShape& g, int c) {
-  int k = 0;
-  if (c < g.grid)
-    for (int rd = 0; rd < g.dp_rounds && c + rd * g.grid < g.split_first; ++rd) ++k;
-  if (c < g.split_ctas) ++k;
-  return k;
-}
 
 // Token range [t0, t1) of piece s (a tile of BN tokens, or one CTA's run of a
 // split tile, as split_reduce_tile cuts it).
@@ -92,6 +86,12 @@ template <typename IO>
 __device__ __forceinline__ void xchg_emit(const XchgArgs& a, uint32_t parity, int t, int n0, uint4 piece) {
   const CommDev& cm = a.cm;
   const int H = a.g.N, T = a.g.T;
+  if (a.nvls) {
+    // this device's partials [T][H], reduced later through the multicast view
+    IO* base = reinterpret_cast<IO*>(a.nv_uc + parity * a.nv_parity_bytes);
+    *reinterpret_cast<uint4*>(base + static_cast<size_t>(t) * H + n0) = piece;
+    return;
+  }
   if (a.oneshot) {
     // slots of every rank: [src rank][T][H]
     const size_t off = (static_cast<size_t>(cm.rank) * T + t) * H + n0;
@@ -110,51 +110,6 @@ __device__ __forceinline__ void xchg_emit(const XchgArgs& a, uint32_t parity, in
   }
 }
 
-// Publish "this CTA delivered `pieces` pieces in call e" into flag row
-// `row` of every rank's reduce-scatter (rs) or all-gather (ag) area. The
-// caller has synchronised the threads that stored the data; one system-scope
-// fence orders all of it before the relaxed flag stores.
-__device__ __forceinline__ void xchg_publish(const CommDev& cm, bool rs, int row, uint32_t e, int pieces) {
-  fence_acq_rel_sys();
-  const uint32_t v = xchg_pack(e, static_cast<uint32_t>(pieces));
-  for (int d = 0; d < cm.world; ++d) {
-    uint32_t* f = rs ? xchg_rs_flags(cm, d) : xchg_ag_flags(cm, d);
-    st_relaxed_sys(f + static_cast<size_t>(row) * kXchgMaxCtas + blockIdx.x, v);
-  }
-}
-
-constexpr int kFlagsPerThread = 8;  // flags one thread polls in the final wait
-
-// Bounded wait of the calling thread until flags f(j) reach want(j) for the
-// j set in `pending` (j < kFlagsPerThread, epoch-wrapping comparison). The
-// polls are relaxed loads, all in flight together; one acquire fence
-// follows, so the thread's later reads see what the flags' writers
-// published. Returns false on timeout (recorded) or when another CTA
-// recorded an error.
-template <typename FlagOf, typename WantOf>
-__device__ __forceinline__ bool xchg_wait_set(uint32_t pending, FlagOf&& flag_of, WantOf&& want_of,
-                                              const CommDev& cm, uint64_t budget_ns) {
-  Deadline d(budget_ns);
-  volatile int* st = cm.status;
-  while (pending != 0u) {
-    uint32_t v[kFlagsPerThread];
-#pragma unroll
-    for (int j = 0; j < kFlagsPerThread; ++j)
-      if (pending & (1u << j)) v[j] = ld_relaxed_sys(flag_of(j));
-#pragma unroll
-    for (int j = 0; j < kFlagsPerThread; ++j)
-      if ((pending & (1u << j)) && epoch_reached(v[j], want_of(j))) pending &= ~(1u << j);
-    if (pending == 0u) break;
-    if (d.expired()) {
-      record_error(cm.status, kDevTimeoutPeer);
-      return false;
-    }
-    if ((d.n & 255u) == 0u && *st != 0) return false;
-  }
-  fence_acq_rel_sys();
-  return true;
-}
-
 template <typename IO, int BN, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
     row_xchg_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -164,7 +119,6 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
   __shared__ uint32_t s_epoch;
   __shared__ uint64_t s_epoch_bar;  // the producer publishes s_epoch after pdl_wait()
   __shared__ float s_red[32];
-  __shared__ int s_ok;
   GemmCtl c = gemm_carve_smem<BN, STAGES>(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -222,7 +176,7 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
     const int etid = epi_tid();
     if (etid == 0) trace(1001);
     const IO* bias = static_cast<const IO*>(a.bias);
-    int acc = 0, done = 0;
+    int acc = 0, done = 0;  // pieces finished (traces only)
     uint32_t acc_phase = 0;
     SegIter it(g);
     Seg tc;
@@ -257,11 +211,8 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
         acc = 0;
         acc_phase ^= 1u;
       }
+      if (etid == 0 && done == 0) trace(1003);
       ++done;
-      named_bar_sync(1, kEpiThreads);  // every thread's stores of this piece issued
-      if (etid == 0 && done == 1) trace(1003);
-      if (etid == 0) xchg_publish(cm, true, cm.rank, e, done);
-      if (etid == 0 && done == 1) trace(1004);
     }
   }
 
@@ -282,108 +233,103 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
   // CTA-uniform: every thread of the CTA takes the same branches below.
   bool ok = __syncthreads_and(*reinterpret_cast<volatile int*>(g.status) == 0) != 0;
 
-  // Step 2 (two-shot): reduce this rank's slice of each of this CTA's pieces.
-  if (!a.oneshot) {
-    const int F = a.fslice, W = H / n, per_tok = F / 8;
-    const IO* slots = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes);
-    const size_t src_stride = static_cast<size_t>(T) * W;
-    SegIter it(g);
-    Seg sg;
-    int k = 0;
-    const uint32_t* rs_mine = xchg_rs_flags(cm, cm.rank) + blockIdx.x;
-    while (ok && it.next(g, sg)) {
-      ++k;
-      // Thread r waits for rank r's delivery of this piece.
-      int wok = 1;
-      if (static_cast<int>(threadIdx.x) < n) {
-        const uint32_t want = xchg_pack(e, static_cast<uint32_t>(k));
-        wok = xchg_wait_set(
-                  1u, [&](int) { return rs_mine + static_cast<size_t>(threadIdx.x) * kXchgMaxCtas; },
-                  [&](int) { return want; }, cm, cm.timeout_ns)
-                  ? 1
-                  : 0;
-      }
-      ok = __syncthreads_and(wok) != 0;
-      if (!ok) break;
-      if (threadIdx.x == 0 && k == 1) trace(1005);
-      int t0, t1;
-      piece_tokens(g, sg, BN, t0, t1);
-      const int items = (t1 - t0) * per_tok;
+  // Barrier 0: every rank's step-1 stores have landed. Every CTA calls each
+  // barrier, errors or not, so the arrival counters stay balanced.
+  if (a.nvls) fence_proxy_alias();  // unicast stores before multicast reads
+  ok = grid_cross_barrier(cm, kBarPartials, e, true) && ok;
+  if (threadIdx.x == 0) trace(1004);
+
+  // NVLS: rank s sums the s-th share of the [T][H] partials over every GPU in
+  // the switch (f32 accumulation, one rounding) and stores it into every
+  // GPU's reduced region with one multicast store.
+  if (a.nvls) {
+    if (ok) {
+      const size_t nvec = static_cast<size_t>(T) * H / 8;
+      const size_t per = (nvec + n - 1) / n;
+      const size_t v0 = static_cast<size_t>(cm.rank) * per;
+      const size_t v1 = v0 + per < nvec ? v0 + per : nvec;
+      const uint8_t* part = a.nv_mc + parity * a.nv_parity_bytes;
+      uint8_t* red = a.nv_mc + parity * a.nv_parity_bytes + a.nv_parity_bytes / 2;
+      const size_t nthr = static_cast<size_t>(gridDim.x) * blockDim.x;
 #pragma unroll 1
-      for (int i = threadIdx.x; i < items; i += blockDim.x) {
-        const int t = t0 + i / per_tok, f8 = i - (i / per_tok) * per_tok;
-        const IO* src = slots + static_cast<size_t>(t) * W + sg.p * F + f8 * 8;
-        uint4 sv[PGB_MAX_RANKS];
-#pragma unroll
-        for (int r = 0; r < PGB_MAX_RANKS; ++r)
-          if (r < n) sv[r] = __ldcg(reinterpret_cast<const uint4*>(src + r * src_stride));
-        float s8[8], p8[8];
-        unpack8_io<IO>(sv[0], s8);
-#pragma unroll
-        for (int r = 1; r < PGB_MAX_RANKS; ++r) {
-          if (r < n) {
-            unpack8_io<IO>(sv[r], p8);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) s8[j] += p8[j];
-          }
-        }
-        const size_t yoff = static_cast<size_t>(t) * H + sg.p * kTileP + cm.rank * F + f8 * 8;
-        for (int d = 0; d < n; ++d)
-          store8<IO>(reinterpret_cast<IO*>(cm.results[d] + parity * cm.result_parity_bytes) + yoff, s8);
+      for (size_t v = v0 + static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < v1; v += nthr) {
+        const uint4 sum = std::is_same<IO, __nv_bfloat16>::value ? multimem_ld_reduce_bf16x8(part + v * 16)
+                                                                  : multimem_ld_reduce_f16x8(part + v * 16);
+        multimem_st_16(red + v * 16, sum);
       }
-      __syncthreads();
-      if (threadIdx.x == 0) xchg_publish(cm, false, cm.rank, e, k);
-      if (threadIdx.x == 0 && k == 1) trace(1006);
+      fence_proxy_alias();
     }
+    ok = grid_cross_barrier(cm, kBarResults, e, true) && ok;
+    fence_proxy_alias();  // multicast stores before unicast reads
   }
 
-  // Step 3: residual add + RMSNorm of the rows this CTA owns, once every
-  // rank's contribution to every piece has arrived.
-  const bool warp_rows = T > static_cast<int>(gridDim.x);
-  if (ok && (warp_rows || static_cast<int>(blockIdx.x) < T)) {
-    // Thread i waits for flags i, i + blockDim.x, ... of the n x gridDim.x
-    // (source rank, CTA) flags, skipping CTAs without pieces.
-    const uint32_t* fl = a.oneshot ? xchg_rs_flags(cm, cm.rank) : xchg_ag_flags(cm, cm.rank);
-    const int nflags = n * static_cast<int>(gridDim.x);
-    const int grid = static_cast<int>(gridDim.x);
-    auto idx = [&](int j) { return static_cast<int>(threadIdx.x) + j * static_cast<int>(blockDim.x); };
-    uint32_t need = 0u;  // CTAs without pieces never publish
-    for (int j = 0; j < kFlagsPerThread && idx(j) < nflags; ++j)
-      if (cta_pieces(g, idx(j) % grid) > 0) need |= 1u << j;
-    const int wok = xchg_wait_set(
-                        need,
-                        [&](int j) {
-                          const int i = idx(j), src = i / grid;
-                          return fl + static_cast<size_t>(src) * kXchgMaxCtas + (i - src * grid);
-                        },
-                        [&](int j) { return xchg_pack(e, static_cast<uint32_t>(cta_pieces(g, idx(j) % grid))); },
-                        cm, cm.timeout_ns)
-                        ? 1
-                        : 0;
-    ok = __syncthreads_and(wok) != 0;
-    if (threadIdx.x == 0) trace(1007);
+  // Step 2 (two-shot): reduce this rank's slice of each of this CTA's pieces
+  // and store it into every rank's y buffer.
+  if (!a.oneshot && !a.nvls) {
     if (ok) {
-      const IO* base = a.oneshot ? reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes)
-                                 : reinterpret_cast<const IO*>(cm.results[cm.rank] + parity * cm.result_parity_bytes);
-      const int nsrc = a.oneshot ? n : 1;
-      const size_t stride = static_cast<size_t>(T) * H;
-      bool done_warp = false;
-      if constexpr (BN >= 128) {
-        constexpr size_t kRing = static_cast<size_t>(STAGES) * GemmSmem<BN, STAGES>::kStageBytes;
-        if (warp_rows && static_cast<size_t>(H) * (4u * (kGemmThreads / 32) + 2u) <= kRing) {
-          reduce_rows_warp_src<IO>(
-              cm, parity, [&](int t) { return base + static_cast<size_t>(t) * H; }, stride, nsrc, false, 0, T, H,
-              out, residual, norm_w, a.eps, a.do_norm, c.a);
-          done_warp = true;
+      const int F = a.fslice, W = H / n, per_tok = F / 8;
+      const IO* slots = reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes);
+      const size_t src_stride = static_cast<size_t>(T) * W;
+      SegIter it(g);
+      Seg sg;
+      while (it.next(g, sg)) {
+        int t0, t1;
+        piece_tokens(g, sg, BN, t0, t1);
+        const int items = (t1 - t0) * per_tok;
+#pragma unroll 1
+        for (int i = threadIdx.x; i < items; i += blockDim.x) {
+          const int t = t0 + i / per_tok, f8 = i - (i / per_tok) * per_tok;
+          const IO* src = slots + static_cast<size_t>(t) * W + sg.p * F + f8 * 8;
+          uint4 sv[PGB_MAX_RANKS];
+#pragma unroll
+          for (int r = 0; r < PGB_MAX_RANKS; ++r)
+            if (r < n) sv[r] = __ldcg(reinterpret_cast<const uint4*>(src + r * src_stride));
+          float s8[8], p8[8];
+          unpack8_io<IO>(sv[0], s8);
+#pragma unroll
+          for (int r = 1; r < PGB_MAX_RANKS; ++r) {
+            if (r < n) {
+              unpack8_io<IO>(sv[r], p8);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) s8[j] += p8[j];
+            }
+          }
+          const size_t yoff = static_cast<size_t>(t) * H + sg.p * kTileP + cm.rank * F + f8 * 8;
+          for (int d = 0; d < n; ++d)
+            store8<IO>(reinterpret_cast<IO*>(cm.results[d] + parity * cm.result_parity_bytes) + yoff, s8);
         }
       }
-      if (!done_warp) {
-        float* srow = reinterpret_cast<float*>(c.a);
-#pragma unroll 1
-        for (int t = blockIdx.x; t < T; t += gridDim.x)
-          reduce_row_src<IO, kXchgRowMaxVec>(cm, parity, base + static_cast<size_t>(t) * H, stride, nsrc, false, t,
-                                             H, out, residual, norm_w, a.eps, a.do_norm, s_red, srow);
+    }
+    if (threadIdx.x == 0) trace(1006);
+    ok = grid_cross_barrier(cm, kBarResults, e, true) && ok;
+  }
+
+  // Step 3: residual add + RMSNorm of the rows this CTA owns.
+  if (threadIdx.x == 0) trace(1007);
+  const bool warp_rows = T > static_cast<int>(gridDim.x);
+  if (ok && (warp_rows || static_cast<int>(blockIdx.x) < T)) {
+    const IO* base =
+        a.nvls ? reinterpret_cast<const IO*>(a.nv_uc + parity * a.nv_parity_bytes + a.nv_parity_bytes / 2)
+        : a.oneshot ? reinterpret_cast<const IO*>(cm.slots[cm.rank] + parity * cm.slot_parity_bytes)
+                    : reinterpret_cast<const IO*>(cm.results[cm.rank] + parity * cm.result_parity_bytes);
+    const int nsrc = (a.oneshot && !a.nvls) ? n : 1;
+    const size_t stride = static_cast<size_t>(T) * H;
+    bool done_warp = false;
+    if constexpr (BN >= 128) {
+      constexpr size_t kRing = static_cast<size_t>(STAGES) * GemmSmem<BN, STAGES>::kStageBytes;
+      if (warp_rows && static_cast<size_t>(H) * (4u * (kGemmThreads / 32) + 2u) <= kRing) {
+        reduce_rows_warp_src<IO>(
+            cm, parity, [&](int t) { return base + static_cast<size_t>(t) * H; }, stride, nsrc, false, 0, T, H, out,
+            residual, norm_w, a.eps, a.do_norm, c.a);
+        done_warp = true;
       }
+    }
+    if (!done_warp) {
+      float* srow = reinterpret_cast<float*>(c.a);
+#pragma unroll 1
+      for (int t = blockIdx.x; t < T; t += gridDim.x)
+        reduce_row_src<IO, kXchgRowMaxVec>(cm, parity, base + static_cast<size_t>(t) * H, stride, nsrc, false, t, H,
+                                           out, residual, norm_w, a.eps, a.do_norm, s_red, srow);
     }
   }
   if (threadIdx.x == 0) trace(1008);
@@ -436,8 +382,7 @@ int dispatch_xchg(pgb_comm* comm, int bn, const XchgArgs& args, const void* x, c
 int row_xchg(pgb_comm* comm, const void* x_local, const void* w_local, const void* bias, void* residual,
              const void* norm_w, float eps, void* out, int T, int N, int K_local, int dtype, void* stream) {
   const int n = comm->world;
-  if (n < 2 || T > 256 || comm->sm_count > kXchgMaxCtas || n * comm->sm_count > kFlagsPerThread * kGemmThreads ||
-      (dtype != PGB_BF16 && dtype != PGB_F16))
+  if (n < 2 || T > 256 || (dtype != PGB_BF16 && dtype != PGB_F16))
     return PGB_ERR_UNSUPPORTED;
   const double S = 2.0 * T * N;
   const bool can_one = static_cast<double>(n) * S <= static_cast<double>(comm->slot_parity_bytes);
@@ -446,7 +391,10 @@ int row_xchg(pgb_comm* comm, const void* x_local, const void* w_local, const voi
   const bool can_two = kTileP % n == 0 && (kTileP / n) % 8 == 0 && N % kTileP == 0 &&
                        S <= static_cast<double>(comm->slot_parity_bytes) &&
                        S <= static_cast<double>(comm->result_parity_bytes);
-  if (!can_one && !can_two) return PGB_ERR_UNSUPPORTED;
+  // NVLS: partials of S bytes per rank in the multicast-bound region.
+  const bool nvls = comm->exchange_mode == PGB_XCHG_NVLS && comm->nvls && N % 8 == 0 &&
+                    S <= static_cast<double>(comm->nv_parity_bytes / 2);
+  if (!can_one && !can_two && !nvls) return PGB_ERR_UNSUPPORTED;
   // One-shot sends (n - 1) S per rank in one hop; two-shot 2 (n - 1) / n S
   // in two hops (one more flag round trip, ~2 us measured on NVLink).
   constexpr double kBw = 700e9, kHop = 2e-6;
@@ -477,6 +425,10 @@ int row_xchg(pgb_comm* comm, const void* x_local, const void* w_local, const voi
   args.g.xchg = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
   args.g.wait_ns = 2000000000ull;
   args.cm = comm_dev(comm);
+  args.nvls = nvls ? 1 : 0;
+  args.nv_uc = reinterpret_cast<uint8_t*>(comm->nv_uc);
+  args.nv_mc = reinterpret_cast<uint8_t*>(comm->nv_mc);
+  args.nv_parity_bytes = comm->nv_parity_bytes;
   args.oneshot = one ? 1 : 0;
   args.fslice = kTileP / n;
   args.out = out;

@@ -359,6 +359,36 @@ __device__ __forceinline__ uint32_t atom_add_acqrel_gpu(uint32_t* p, uint32_t v)
   return old;
 }
 
+// ------------------------------------------------------- NVLink multicast ---
+// 8 x 16-bit values at multicast address mc summed over every GPU of the
+// team in the switch, accumulated in f32 and rounded once to the element type.
+__device__ __forceinline__ uint4 multimem_ld_reduce_bf16x8(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(reinterpret_cast<uint64_t>(mc))
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 multimem_ld_reduce_f16x8(const void* mc) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(reinterpret_cast<uint64_t>(mc))
+               : "memory");
+  return v;
+}
+// 16 bytes stored at multicast address mc on every GPU of the team.
+__device__ __forceinline__ void multimem_st_16(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(reinterpret_cast<uint64_t>(mc)),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// Orders this thread's accesses made through one virtual alias of a memory
+// location (the unicast view) with those made through another (the
+// multicast view).
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
 // Signed distance between two wrapping epoch counters.
 __device__ __forceinline__ bool epoch_reached(uint32_t seen, uint32_t want) {
   return static_cast<int32_t>(seen - want) >= 0;

@@ -119,6 +119,7 @@ class PGBCommunicator:
         _lib.call("pgb_comm_create", rank, world_size, max_bytes, ubuf, device, ctypes.byref(handle))
         self._h = handle
         self._closed = False
+        self.nvls = False  # NVLink multicast region bound (setup_nvls)
 
     # -- peer exchange ------------------------------------------------------
     def export_handle(self) -> bytes:
@@ -164,10 +165,11 @@ class PGBCommunicator:
 
     def set_exchange_mode(self, mode: str) -> None:
         """Multi-rank decode row ops: "auto" (the default, the grid-barrier
-        kernel), "oneshot" / "twoshot" (the per-piece exchange kernel) or
-        "barrier"."""
+        kernel), "oneshot" / "twoshot" (the slice-exchange kernel), "barrier",
+        or "nvls" (NVLink multicast reduce; needs a communicator made with
+        nvls=True on hardware that supports it, else "auto")."""
         codes = {"auto": _lib.PGB_XCHG_AUTO, "oneshot": _lib.PGB_XCHG_ONESHOT, "twoshot": _lib.PGB_XCHG_TWOSHOT,
-                 "barrier": _lib.PGB_XCHG_BARRIER}
+                 "barrier": _lib.PGB_XCHG_BARRIER, "nvls": _lib.PGB_XCHG_NVLS}
         if mode not in codes:
             raise ValueError(f"unknown exchange mode {mode!r}; expected one of {sorted(codes)}")
         _lib.call("pgb_comm_set_exchange_mode", self._h, codes[mode])
@@ -202,9 +204,77 @@ class PGBCommunicator:
             pass
 
 
+def _all_ok(flag: bool, group) -> bool:
+    import torch.distributed as dist
+
+    t = torch.tensor([1 if flag else 0], dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return bool(t.item())
+
+
+def setup_nvls(comm: PGBCommunicator, tp_rank: int, tp_size: int, tp_cpu_group, uid: bytes) -> bool:
+    """Bind an NVLink multicast region to every rank of `comm` (see
+    pgb_comm_nvls_create in include/pgb.h). Rank 0 creates the multicast
+    object; its POSIX file descriptor reaches the other rank processes over an
+    abstract Unix socket (SCM_RIGHTS) named after the communicator's uid. Every
+    phase ends with an all-ranks agreement on the CPU group, so either every
+    rank ends with the region bound (returns True) or none uses it (False)."""
+    import os
+    import socket
+
+    lib = _lib.load()
+    sup = ctypes.c_int(0)
+    _lib.call("pgb_comm_nvls_supported", comm.handle, ctypes.byref(sup))
+    if not _all_ok(bool(sup.value), tp_cpu_group):
+        return False
+    name = b"\0pgb-nvls-" + uid[:16].hex().encode()
+    fd = -1
+    if tp_rank == 0:
+        fdc = ctypes.c_int(-1)
+        created = lib.pgb_comm_nvls_create(comm.handle, ctypes.byref(fdc)) == 0
+        srv = None
+        if created:
+            fd = fdc.value
+            srv = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+            srv.settimeout(120)
+            srv.bind(name)
+            srv.listen(tp_size)
+        go = _all_ok(created, tp_cpu_group)  # the others connect only now
+        try:
+            if go:
+                for _ in range(tp_size - 1):
+                    conn, _ = srv.accept()
+                    with conn:
+                        socket.send_fds(conn, [b"f"], [fd])
+        finally:
+            if srv is not None:
+                srv.close()
+        if not go:
+            if fd >= 0:
+                os.close(fd)
+            return False
+    else:
+        if not _all_ok(True, tp_cpu_group):
+            return False
+        with socket.socket(socket.AF_UNIX, socket.SOCK_STREAM) as cl:
+            cl.settimeout(120)
+            cl.connect(name)
+            _, fds, _, _ = socket.recv_fds(cl, 16, 1)
+        fd = fds[0]
+    added = lib.pgb_comm_nvls_add(comm.handle, fd) == 0
+    os.close(fd)
+    if not _all_ok(added, tp_cpu_group):
+        return False
+    bound = lib.pgb_comm_nvls_bind(comm.handle) == 0
+    comm.nvls = _all_ok(bound, tp_cpu_group)
+    return comm.nvls
+
+
 def init_comm(*, tp_rank: int, tp_size: int, tp_cpu_group, max_size_bytes: int = 0,
-              device: int | None = None) -> PGBCommunicator:
-    """Create and connect a communicator over the CPU group (init_pynccl, pynccl.py:39-71)."""
+              device: int | None = None, nvls: bool = False) -> PGBCommunicator:
+    """Create and connect a communicator over the CPU group (init_pynccl,
+    pynccl.py:39-71). nvls=True also binds an NVLink multicast region where
+    every device supports it (comm.nvls tells whether it did)."""
     import torch.distributed as dist
 
     ids = [create_uid()] if tp_rank == 0 else [None]
@@ -218,6 +288,8 @@ def init_comm(*, tp_rank: int, tp_size: int, tp_cpu_group, max_size_bytes: int =
         dist.all_gather_object(handles, comm.export_handle(), group=tp_cpu_group)
         comm.open_peers(handles)
         dist.barrier(group=tp_cpu_group)
+        if nvls:
+            setup_nvls(comm, tp_rank, tp_size, tp_cpu_group, uid)
     return comm
 
 
@@ -274,10 +346,11 @@ class DistributedCommunicator:
         return cls.impl.all_gather(x)
 
 
-def enable_pgb_distributed(tp_info: DistributedInfo, tp_cpu_group, max_bytes: int) -> PGBCommunicator:
+def enable_pgb_distributed(tp_info: DistributedInfo, tp_cpu_group, max_bytes: int,
+                           nvls: bool = False) -> PGBCommunicator:
     """enable_pynccl_distributed (impl.py:65-80) for the libpgb communicator."""
     comm = init_comm(tp_rank=tp_info.rank, tp_size=tp_info.size, tp_cpu_group=tp_cpu_group,
-                     max_size_bytes=max_bytes)
+                     max_size_bytes=max_bytes, nvls=nvls)
     DistributedCommunicator.impl = PGBDistributedImpl(comm=comm)
     DistributedCommunicator.comm = comm
     return comm

@@ -70,8 +70,12 @@ def _worker(rank: int, world: int, port: int, case: str, q):
                                 init_method=f"tcp://127.0.0.1:{port}", timeout=timedelta(seconds=120))
         pgb = importlib.import_module("pico-sglang_b200")
         D = importlib.import_module("pico-sglang_b200.distributed")
+        # The fused case also binds an NVLink multicast region where the
+        # devices support it; the timeout case keeps it off (a rank that
+        # leaves while its memory is bound to a multicast object is not a
+        # failure to provoke).
         comm = D.init_comm(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD,
-                           max_size_bytes=64 << 20)
+                           max_size_bytes=64 << 20, nvls=(case == "fused"))
         dev = torch.device("cuda", rank)
         out = {}
         if case == "known_answers":
@@ -107,10 +111,18 @@ def _worker(rank: int, world: int, port: int, case: str, q):
             # Decode shapes under every exchange mode of the multi-rank row op
             # (per-piece one-shot / two-shot, the cost model's pick, and the
             # grid-barrier kernel), then a prefill shape and a ragged one.
-            runs = [(mode, shp) for mode in ("auto", "oneshot", "twoshot", "barrier")
+            import ctypes
+
+            sup = ctypes.c_int(0)
+            pgb._lib.call("pgb_comm_nvls_supported", comm.handle, ctypes.byref(sup))
+            out["nvls_bound_where_supported"] = (comm.nvls == bool(sup.value), f"supported={sup.value} bound={comm.nvls}")
+            modes = ("auto", "oneshot", "twoshot", "barrier") + (("nvls",) if comm.nvls else ())
+            runs = [(mode, shp) for mode in modes
                     for shp in ((1, 4096, 4096), (8, 4096, 12288), (64, 4096, 4096), (256, 4096, 12288),
                                 (64, 5120, 25600))]
             runs += [("auto", (1000, 4096, 2048)), ("auto", (3, 200, 256)), ("twoshot", (3, 200, 256))]
+            if comm.nvls:
+                runs += [("nvls", (3, 200, 256))]
             for mode, (T, H, K) in runs:
                 comm.set_exchange_mode(mode)
                 g = torch.Generator(device=dev).manual_seed(T + H + K)
