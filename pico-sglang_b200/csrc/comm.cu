@@ -131,6 +131,101 @@ __global__ void __launch_bounds__(256) allreduce_kernel(CommDev cm, IO* data, lo
   comm_end(cm, e);
 }
 
+// 16-byte vectors of IO summed element-wise in f32 (rank order) and rounded.
+template <typename IO>
+__device__ __forceinline__ void acc16(float* acc, uint4 v) {
+  if constexpr (std::is_same<IO, float>::value) {
+    acc[0] += __uint_as_float(v.x);
+    acc[1] += __uint_as_float(v.y);
+    acc[2] += __uint_as_float(v.z);
+    acc[3] += __uint_as_float(v.w);
+  } else {
+    float f[8];
+    unpack8_io<IO>(v, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] += f[j];
+  }
+}
+template <typename IO>
+__device__ __forceinline__ uint4 round16(const float* acc) {
+  uint4 out;
+  if constexpr (std::is_same<IO, float>::value) {
+    out = make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]), __float_as_uint(acc[2]), __float_as_uint(acc[3]));
+  } else {
+    IO h[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] = static_cast<IO>(acc[j]);
+    out = *reinterpret_cast<const uint4*>(h);
+  }
+  return out;
+}
+
+// all_reduce on 16-byte vectors (count a multiple of 16 / sizeof(IO), data
+// 16-byte aligned); same phases and slot layout as allreduce_kernel, in
+// vectors: `nvec` vectors, two-shot owners hold `per` vectors each.
+template <typename IO>
+__global__ void __launch_bounds__(256) allreduce_vec_kernel(CommDev cm, uint4* data, long long nvec, long long per,
+                                                            int oneshot) {
+  constexpr int kVecElems = 16 / static_cast<int>(sizeof(IO));
+  __shared__ uint32_t s_epoch;
+  pdl_wait();
+  if (threadIdx.x == 0) s_epoch = comm_begin(cm);
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const uint32_t parity = e & 1u;
+  const long long cap = oneshot ? nvec : per;
+  const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
+  auto slot = [&](int d) { return reinterpret_cast<uint4*>(cm.slots[d] + parity * cm.slot_parity_bytes); };
+  auto result = [&](int d) { return reinterpret_cast<uint4*>(cm.results[d] + parity * cm.result_parity_bytes); };
+
+  // Phase 1: this rank's vectors into the reducing ranks' slots.
+#pragma unroll 1
+  for (long long i = tid; i < nvec; i += nthr) {
+    const uint4 v = __ldcg(data + i);
+    if (oneshot) {
+      for (int d = 0; d < cm.world; ++d) slot(d)[cm.rank * cap + i] = v;
+    } else {
+      const int o = static_cast<int>(i / per);
+      slot(o)[cm.rank * cap + (i - o * per)] = v;
+    }
+  }
+  const bool ok = grid_cross_barrier(cm, kBarPartials, e, true);
+  // Phase 2: reduce the owned range in rank order; write locally and push.
+  const long long lo = oneshot ? 0 : min(nvec, cm.rank * per);
+  const long long hi = oneshot ? nvec : min(nvec, (cm.rank + 1) * per);
+  if (ok) {
+    const uint4* mine = slot(cm.rank);
+#pragma unroll 1
+    for (long long i = lo + tid; i < hi; i += nthr) {
+      uint4 sv[PGB_MAX_RANKS];
+#pragma unroll
+      for (int r = 0; r < PGB_MAX_RANKS; ++r)
+        if (r < cm.world) sv[r] = __ldcg(mine + r * cap + (i - lo));
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < PGB_MAX_RANKS; ++r)
+        if (r < cm.world) acc16<IO>(acc, sv[r]);
+      const uint4 out = round16<IO>(acc);
+      data[i] = out;
+      if (!oneshot)
+        for (int d = 0; d < cm.world; ++d)
+          if (d != cm.rank) result(d)[i] = out;
+    }
+  }
+  if (!oneshot) {
+    const bool ok2 = grid_cross_barrier(cm, kBarResults, e, true);
+    if (ok && ok2) {
+      const uint4* res = result(cm.rank);
+#pragma unroll 1
+      for (long long i = tid; i < nvec; i += nthr)
+        if (i < lo || i >= hi) data[i] = __ldcg(res + i);
+    }
+  }
+  comm_end(cm, e);
+  (void)kVecElems;
+}
+
 // ------------------------------------------------------------- all_gather --
 template <typename IO>
 __global__ void __launch_bounds__(256) allgather_kernel(CommDev cm, IO* out, const IO* in,
@@ -163,6 +258,37 @@ __global__ void __launch_bounds__(256) allgather_kernel(CommDev cm, IO* out, con
   comm_end(cm, e);
 }
 
+// all_gather on 16-byte vectors: in[count] of every rank to out, where a
+// rank's block starts at out + r * out_stride + out_offset (all in vectors).
+__global__ void __launch_bounds__(256) allgather_vec_kernel(CommDev cm, uint4* out, const uint4* in, long long nvec,
+                                                            long long out_stride, long long out_offset) {
+  __shared__ uint32_t s_epoch;
+  pdl_wait();
+  if (threadIdx.x == 0) s_epoch = comm_begin(cm);
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const uint32_t parity = e & 1u;
+  const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
+#pragma unroll 1
+  for (long long i = tid; i < nvec; i += nthr) {
+    const uint4 v = __ldcg(in + i);
+    for (int d = 0; d < cm.world; ++d)
+      reinterpret_cast<uint4*>(cm.results[d] + parity * cm.result_parity_bytes)[cm.rank * nvec + i] = v;
+  }
+  const bool ok = grid_cross_barrier(cm, kBarPartials, e, true);
+  if (ok) {
+    const uint4* res = reinterpret_cast<const uint4*>(cm.results[cm.rank] + parity * cm.result_parity_bytes);
+    const long long total = nvec * cm.world;
+#pragma unroll 1
+    for (long long i = tid; i < total; i += nthr) {
+      const long long r = i / nvec, j = i - r * nvec;
+      out[r * out_stride + out_offset + j] = __ldcg(res + i);
+    }
+  }
+  comm_end(cm, e);
+}
+
 template <typename K, typename... Args>
 int launch_coop(K kern, int grid, cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg{};
@@ -188,6 +314,28 @@ template <typename IO>
 int all_reduce_typed(pgb_comm* c, IO* data, size_t count, cudaStream_t s) {
   const size_t elem = sizeof(IO);
   const int n = c->world;
+  constexpr size_t kVec = 16 / sizeof(IO);
+  if (count % kVec == 0 && (reinterpret_cast<uintptr_t>(data) & 15u) == 0u) {
+    // 16-byte vectors: chunks whose two-shot slots [n][per] and result copy fit.
+    size_t max_vec = std::min(c->slot_parity_bytes, c->result_parity_bytes) / 16;
+    const size_t nvec_all = count / kVec;
+    for (size_t off = 0; off < nvec_all; off += max_vec) {
+      const size_t cnt = std::min(max_vec, nvec_all - off);
+      const size_t per = (cnt + n - 1) / n;
+      const double S = static_cast<double>(cnt) * 16.0;
+      const int oneshot = (n * S <= static_cast<double>(c->slot_parity_bytes)) &&
+                          ((n - 1) * S / 770e9 + n * S / 6.5e12 <= 2.0 * (n - 1) / n * S / 770e9 + S / 6.5e12 + 2e-6);
+      if (!oneshot && static_cast<double>(n) * per * 16.0 > static_cast<double>(c->slot_parity_bytes))
+        return set_error(PGB_ERR_INVALID, "all_reduce: chunk does not fit the slots");
+      const long long work = static_cast<long long>(oneshot ? cnt : per);
+      int grid = static_cast<int>(std::min<long long>(c->sm_count, (work + 255) / 256));
+      if (grid < 1) grid = 1;
+      int rc = launch_coop(allreduce_vec_kernel<IO>, grid, s, comm_dev(c), reinterpret_cast<uint4*>(data) + off,
+                           static_cast<long long>(cnt), static_cast<long long>(per), oneshot);
+      if (rc) return rc;
+    }
+    return PGB_OK;
+  }
   // Largest chunk whose two-shot slots [n][per] and result copy fit.
   size_t max_chunk = std::min(c->slot_parity_bytes / elem, c->result_parity_bytes / elem);
   max_chunk = max_chunk / 8 * 8;
@@ -213,6 +361,22 @@ int all_reduce_typed(pgb_comm* c, IO* data, size_t count, cudaStream_t s) {
 template <typename IO>
 int all_gather_typed(pgb_comm* c, IO* out, const IO* in, size_t count, cudaStream_t s) {
   const size_t elem = sizeof(IO);
+  constexpr size_t kVec = 16 / sizeof(IO);
+  if (count % kVec == 0 && ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(in)) & 15u) == 0u) {
+    const size_t nvec_all = count / kVec;
+    const size_t max_vec = c->result_parity_bytes / 16 / c->world;
+    if (max_vec == 0) return set_error(PGB_ERR_INVALID, "all_gather: buffer too small");
+    for (size_t off = 0; off < nvec_all; off += max_vec) {
+      const size_t cnt = std::min(max_vec, nvec_all - off);
+      int grid = static_cast<int>(std::min<long long>(c->sm_count, (static_cast<long long>(cnt) * c->world + 255) / 256));
+      if (grid < 1) grid = 1;
+      int rc = launch_coop(allgather_vec_kernel, grid, s, comm_dev(c), reinterpret_cast<uint4*>(out),
+                           reinterpret_cast<const uint4*>(in) + off, static_cast<long long>(cnt),
+                           static_cast<long long>(nvec_all), static_cast<long long>(off));
+      if (rc) return rc;
+    }
+    return PGB_OK;
+  }
   size_t max_chunk = c->result_parity_bytes / elem / c->world;
   if (max_chunk == 0) return set_error(PGB_ERR_INVALID, "all_gather: buffer too small");
   for (size_t off = 0; off < count; off += max_chunk) {

@@ -113,6 +113,17 @@ def _worker(rank: int, world: int, port: int, case: str, q):
             comm.all_gather(dst, src)
             exp = torch.arange(world, dtype=dtype, device=dev).repeat_interleave(K)
             out["gather"] = bool(torch.equal(dst, exp))
+            # 16-byte vector path (above) and element path (7 elements)
+            for cnt, dt in ((7, torch.bfloat16), (1000, torch.float32), (3 << 20, torch.bfloat16)):
+                src = torch.full((cnt,), rank + 1, dtype=dt, device=dev)
+                dst = torch.empty((cnt * world,), dtype=dt, device=dev)
+                comm.all_gather(dst, src)
+                exp = torch.arange(1, world + 1, dtype=dt, device=dev).repeat_interleave(cnt)
+                out[f"gather_{cnt}_{dt}"] = bool(torch.equal(dst, exp))
+            # a large payload in chunks through the vector path: 96 MiB > the 64 MiB buffer
+            x = torch.full((48 << 20,), float(rank + 1), dtype=torch.bfloat16, device=dev)
+            f(x)
+            out["chunked"] = bool(torch.all(x == world * (world + 1) / 2).item())
             comm.check_status()
         elif case == "fused":
             # Decode shapes under every exchange mode of the multi-rank row op
