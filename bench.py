@@ -285,6 +285,10 @@ def time_graph(ctx: Ctx, graph, steps: int, warmup: int) -> float:
 
 
 def capture(ctx: Ctx, fn):
+    # Inputs are made on the default stream: let that work finish before the
+    # bench stream touches them (the caching allocator hands out blocks that
+    # pending default-stream work may still write).
+    torch.cuda.synchronize()
     with torch.cuda.stream(ctx.stream):
         fn()  # eager warm-up: allocates workspaces (and NCCL state) outside capture
         torch.cuda.synchronize()
@@ -688,6 +692,7 @@ def measure_nvlink(ctx: Ctx, nbytes: int = 256 << 20) -> float | None:
         for r in dist.batch_isend_irecv(ops):
             r.wait()
 
+    torch.cuda.synchronize()
     with torch.cuda.stream(ctx.stream):
         for _ in range(3):
             once()

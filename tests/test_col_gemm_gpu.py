@@ -124,3 +124,42 @@ def test_col_gemm_shapes_share_one_workspace(pgb, cuda_device):
         _check(y, _ref(x, w))
     head = ws[:256 + 8192]
     assert int(head.count_nonzero().item()) == 0, "status word and counters are left zeroed"
+
+
+# Decode shards of config 2 (hidden 4096, intermediate 12288, 32 q / 8 kv heads
+# of 128) at TP = 1, 2, 4, 8: qkv, o, gate_up and down.
+_DECODE_NK = sorted({(n, k) for tp in (1, 2, 4, 8) for n, k in (
+    (6144 // tp, 4096), (4096, 4096 // tp), (24576 // tp, 4096), (4096, 12288 // tp))})
+
+
+def test_col_gemm_decode_sequence_writes_every_element(pgb, cuda_device):
+    """Every decode shard at T = 1, 64, 128, 256, one after another on one
+    stream and one workspace (each plan leaves its own split partials behind
+    for the next), eagerly and as CUDA-graph replays. The output is filled
+    with NaN first: an element that no CTA stores, or a split tile summed
+    from a stale partial, fails the comparison."""
+    stream = torch.cuda.Stream(cuda_device)
+    cases = [(T, n, k) for T in (256, 1, 128, 64) for n, k in _DECODE_NK]
+    g = torch.Generator(device=cuda_device).manual_seed(77)
+    xs = {(T, k): torch.randn(T, k, device=cuda_device, generator=g).bfloat16() for T, _, k in cases}
+    ws = {(n, k): (torch.randn(n, k, device=cuda_device, generator=g) * 0.02).bfloat16() for _, n, k in cases}
+    ys = {c: torch.empty(c[0], c[1], device=cuda_device, dtype=torch.bfloat16) for c in cases}
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for c in cases:  # eager, and sizes the shared workspace before capture
+            ys[c].fill_(float("nan"))
+            pgb.col_gemm(xs[(c[0], c[2])], ws[(c[1], c[2])], out=ys[c])
+        stream.synchronize()
+        for c in cases:
+            _check(ys[c], _ref(xs[(c[0], c[2])], ws[(c[1], c[2])]))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for c in cases:
+                ys[c].fill_(float("nan"))
+                pgb.col_gemm(xs[(c[0], c[2])], ws[(c[1], c[2])], out=ys[c])
+        for _ in range(3):
+            graph.replay()
+        stream.synchronize()
+    for c in cases:
+        _check(ys[c], _ref(xs[(c[0], c[2])], ws[(c[1], c[2])]))
+    del graph
