@@ -281,4 +281,18 @@ extern "C" PGB_API int pgb_debug_set_trace(void* buf) {
   cudaError_t e = cudaMemcpyToSymbol(pgb::pgb_trace_buf, &buf, sizeof(buf));
   return e == cudaSuccess ? 0 : 2;
 }
+
+namespace {
+__global__ void trace_selftest_kernel() { pgb::trace(7); }
+}  // namespace
+
+// Work-build only: reads the pointer back and records slot 7 of CTA 0 from a
+// one-thread kernel. Returns 0 when the pointer read back equals `expect`.
+extern "C" PGB_API int pgb_debug_trace_selftest(void* expect) {
+  void* got = nullptr;
+  if (cudaMemcpyFromSymbol(&got, pgb::pgb_trace_buf, sizeof(got)) != cudaSuccess) return 2;
+  trace_selftest_kernel<<<1, 1>>>();
+  if (cudaDeviceSynchronize() != cudaSuccess) return 3;
+  return got == expect ? 0 : 1;
+}
 #endif

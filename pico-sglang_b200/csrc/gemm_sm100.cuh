@@ -121,22 +121,6 @@ __host__ __device__ __forceinline__ int tile_contributors(const GemmShape& g, in
   return tile >= g.split_first ? g.nsplit : 1;
 }
 
-// Token columns [c0, c1) of a split tile (tile-relative, V real tokens) that
-// split r of S owns: runs of 4-token groups, cut evenly.
-__host__ __device__ __forceinline__ void split_cols(int V, int S, int r, int& c0, int& c1) {
-  const int G = (V + 3) >> 2;
-  c0 = (r * G / S) * 4;
-  c1 = ((r + 1) * G / S) * 4;
-  c0 = c0 < V ? c0 : V;
-  c1 = c1 < V ? c1 : V;
-}
-
-// Bytes of a split CTA's gather area in its ring: S slots (its own and the
-// others' pieces) of its largest column run, 128 f32 per column.
-__host__ __device__ constexpr size_t split_recv_bytes(int BN, int S) {
-  return static_cast<size_t>(S) * static_cast<size_t>((BN / 4 + S - 1) / S) * 4u * 128u * 4u;
-}
-
 // Weight tile of segment s, k-block kb, into dst (the A operand in the swap
 // orientation, B otherwise). In gated mode (g.glu) the weight is the merged
 // [gate; up] matrix of 2 * g.N rows (LinearColParallelMerged's layout,
@@ -193,6 +177,42 @@ __host__ __device__ constexpr int gemm_stages_for(int bn) {
 template <int BN>
 constexpr int gemm_stages() {
   return gemm_stages_for(BN);
+}
+
+// Bytes of the pipeline ring of a tile width (A and B stages).
+__host__ __device__ constexpr size_t gemm_ring_bytes(int bn) {
+  return static_cast<size_t>(gemm_stages_for(bn)) * static_cast<size_t>(kTileP + bn) * kBlockK * 2u;
+}
+
+// Split-K column runs. A split tile's real tokens are cut into nsplit runs of
+// whole units, one per CTA; each CTA sums the S partials of its run. Units of
+// 32 tokens (one epilogue chunk) when the largest run's gather area fits the
+// ring, else 4-token groups (S = 7 at BN = 256, S >= 7 at BN <= 64): with
+// 32-token units every chunk of the partial is wholly one CTA's, which the
+// epilogue moves with constant-offset loads and stores.
+__host__ __device__ constexpr size_t split_recv_bytes_unit(int BN, int S, int unit) {
+  return static_cast<size_t>(S) * static_cast<size_t>(((BN + unit - 1) / unit + S - 1) / S) *
+         static_cast<size_t>(unit) * 128u * 4u;
+}
+__host__ __device__ constexpr int split_unit(int BN, int S) {
+  return split_recv_bytes_unit(BN, S, 32) <= gemm_ring_bytes(BN) ? 32 : 4;
+}
+
+// Token columns [c0, c1) of a split tile of width BN (tile-relative, V real
+// tokens) that split r of S owns: runs of split_unit tokens, cut evenly.
+__host__ __device__ __forceinline__ void split_cols(int BN, int V, int S, int r, int& c0, int& c1) {
+  const int unit = split_unit(BN, S);
+  const int G = (V + unit - 1) / unit;
+  c0 = (r * G / S) * unit;
+  c1 = ((r + 1) * G / S) * unit;
+  c0 = c0 < V ? c0 : V;
+  c1 = c1 < V ? c1 : V;
+}
+
+// Bytes of a split CTA's gather area in its ring: S slots (its own and the
+// others' pieces) of its largest column run, 128 f32 per column.
+__host__ __device__ constexpr size_t split_recv_bytes(int BN, int S) {
+  return split_recv_bytes_unit(BN, S, split_unit(BN, S));
 }
 
 struct GemmCtl {
@@ -374,6 +394,7 @@ __device__ __forceinline__ void gemm_mma(const GemmShape& g, const GemmCtl& c, u
     }
     if (!ok) break;
     umma_commit(&c.acc_full[acc]);
+    trace(404);
     if (++acc == 2) {
       acc = 0;
       acc_phase ^= 1u;
@@ -591,7 +612,7 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
   const size_t slab = static_cast<size_t>(BN) * kTileP;
   uint32_t* ctr = g.ctr + 2 * u;
   int my0, my1;
-  split_cols(V, S, j, my0, my1);
+  split_cols(BN, V, S, j, my0, my1);
   bool ok = true;
 
   // 1. This CTA's partial: the other CTAs' columns to its exchange slab, its
@@ -601,24 +622,41 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
   float* recv = reinterpret_cast<float*>(c.a);
   float* mine = g.xchg + static_cast<size_t>(u * S + j) * slab;
   float* own = recv + static_cast<size_t>(j) * n_mine * kTileP + row;
+  if (tid == 0) trace(400);
 #pragma unroll 1
   for (int cb = 0; cb < V; cb += 32) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, cb), r);
     tmem_ld_wait();
+    if (tid == 0 && cb < 128) trace(405 + (cb >> 4));
+    if (cb >= my0 && cb + 32 <= my1) {
+      // The whole chunk is this CTA's: park it in its slot of the gather area.
+      float* o = own + static_cast<size_t>(cb - my0) * kTileP;
 #pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const int col = cb + jj;
-      const float x = __uint_as_float(r[jj]);
-      const bool is_mine = col >= my0 && col < my1;
-      if (is_mine) own[static_cast<size_t>(col - my0) * kTileP] = x;
-      if (!is_mine && col < V) __stcg(mine + static_cast<size_t>(col) * kTileP + row, x);
+      for (int jj = 0; jj < 32; ++jj) o[jj * kTileP] = __uint_as_float(r[jj]);
+    } else if ((cb + 32 <= my0 || cb >= my1) && cb + 32 <= V) {
+      // The whole chunk is other CTAs': to this CTA's exchange slab.
+      float* m = mine + static_cast<size_t>(cb) * kTileP + row;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) __stcg(m + jj * kTileP, __uint_as_float(r[jj]));
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int col = cb + jj;
+        const float x = __uint_as_float(r[jj]);
+        const bool is_mine = col >= my0 && col < my1;
+        if (is_mine) own[static_cast<size_t>(col - my0) * kTileP] = x;
+        if (!is_mine && col < V) __stcg(mine + static_cast<size_t>(col) * kTileP + row, x);
+      }
     }
+    if (tid == 0 && cb < 128) trace(406 + (cb >> 4));
   }
   // bar.sync, then one gpu-scope release: every thread's stores are ordered
   // before the publication.
+  if (tid == 0) trace(402);
   named_bar_sync(1, kEpiThreads);
   if (tid == 0) {
+    trace(403);
     atom_add_acqrel_gpu(ctr, 1u);
     trace(1011);
   }
@@ -672,13 +710,25 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
       const int lim = n_mine - 1 - c0;
       float v[32];
       const float* s0 = base + static_cast<size_t>(c0) * kTileP;
+      if (lim >= 31) {
+        // A full chunk: constant offsets.
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) v[jj] = s0[static_cast<size_t>(min(jj, lim)) * kTileP];
+        for (int jj = 0; jj < 32; ++jj) v[jj] = s0[jj * kTileP];
 #pragma unroll 1
-      for (int q = 1; q < S; ++q) {
-        const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
+        for (int q = 1; q < S; ++q) {
+          const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) v[jj] += sq[static_cast<size_t>(min(jj, lim)) * kTileP];
+          for (int jj = 0; jj < 32; ++jj) v[jj] += sq[jj * kTileP];
+        }
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) v[jj] = s0[static_cast<size_t>(min(jj, lim)) * kTileP];
+#pragma unroll 1
+        for (int q = 1; q < S; ++q) {
+          const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) v[jj] += sq[static_cast<size_t>(min(jj, lim)) * kTileP];
+        }
       }
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) v[jj] += bias_v;

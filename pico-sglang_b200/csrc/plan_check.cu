@@ -95,7 +95,7 @@ extern "C" int pgb_check_work_plan(int T, int N, int K, int sms, int all_streamk
     int prev = 0;
     for (int r = 0; r < p.nsplit; ++r) {
       int c0, c1;
-      split_cols(V, p.nsplit, r, c0, c1);
+      split_cols(p.bn, V, p.nsplit, r, c0, c1);
       if (c0 != prev || c1 < c0) return set_error(PGB_ERR_STATE, "tile %d: split columns of %d not contiguous", t, r);
       prev = c1;
     }
@@ -113,7 +113,7 @@ extern "C" int pgb_check_work_plan(int T, int N, int K, int sms, int all_streamk
   if (p.counter_bytes > region)
     return set_error(PGB_ERR_STATE, "counters need %zu bytes, the region holds %zu", p.counter_bytes, region);
   // The gathered pieces must fit the smallest ring of this tile width.
-  const size_t ring = static_cast<size_t>(gemm_stages_for(p.bn)) * (128u + p.bn) * 64u * 2u;
+  const size_t ring = gemm_ring_bytes(p.bn);
   if (p.nsplit > 1 && split_recv_bytes(p.bn, p.nsplit) > ring)
     return set_error(PGB_ERR_STATE, "split of %d gathers %zu bytes, ring holds %zu", p.nsplit,
                      split_recv_bytes(p.bn, p.nsplit), ring);

@@ -71,7 +71,7 @@ __device__ __forceinline__ void piece_tokens(const GemmShape& g, const Seg& s, i
   const int V = min(bn, g.T - base);
   if (s.nctb > 1) {
     int c0, c1;
-    split_cols(V, s.nctb, s.contrib, c0, c1);
+    split_cols(bn, V, s.nctb, s.contrib, c0, c1);
     t0 = base + c0;
     t1 = base + c1;
   } else {

@@ -126,6 +126,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
+// 16-byte asynchronous copy global -> shared through L2 only (cp.async.cg):
+// no registers held while it is in flight. Both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src))
+               : "memory");
+}
+// Waits for every cp.async this thread has issued.
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// 16-byte store that stays in L2 (st.global.cg).
+__device__ __forceinline__ void st_cg_f32x4(float* p, float a, float b, float c, float d) {
+  asm volatile("st.global.cg.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(reinterpret_cast<uint64_t>(p)), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
 // Orders this thread's earlier generic-proxy accesses (and what its acquires
 // made visible) before its later async-proxy accesses to global memory.
 __device__ __forceinline__ void fence_proxy_async_global() {
@@ -200,6 +215,13 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
+}
+// 8 consecutive columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -398,14 +420,21 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as
 
 // Optional pipeline timeline for performance investigation. Compiled only
 // with -DPGB_TRACE; the host sets pgb_trace_buf to a zeroed device buffer of
-// [gridDim.x][kTraceSlots] u64 (ns timestamps). Off in normal builds.
+// [gridDim.x][kTraceSlots] u64 (ns timestamps). Off in normal builds. The
+// pointer has internal linkage: each translation unit's kernels read the copy
+// that its own pgb_debug_set_trace* entry point writes (with external
+// linkage the host-side symbols of the copies were merged and the setter
+// wrote a copy no kernel read).
 #ifdef PGB_TRACE
 constexpr int kTraceSlots = 1024;
-__device__ uint64_t* pgb_trace_buf;
+static __device__ uint64_t* pgb_trace_buf;
 __device__ __forceinline__ void trace(int slot) {
   // Read-only path for the pointer: a trace point must not add a memory
-  // round trip to the code it measures.
-  uint64_t* buf = reinterpret_cast<uint64_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&pgb_trace_buf)));
+  // round trip to the code it measures. The load is inline assembly: device
+  // code never writes the variable, so a plain read may be folded to its
+  // initial value (null).
+  uint64_t* buf;
+  asm volatile("ld.global.nc.u64 %0, [%1];" : "=l"(buf) : "l"(&pgb_trace_buf));
   if (buf != nullptr && slot < kTraceSlots) buf[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = globaltimer_ns();
 }
 #else
