@@ -629,16 +629,30 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
     tmem_ld_32x32b_x32(epi_taddr(tmem, acc, BN, cb), r);
     tmem_ld_wait();
     if (tid == 0 && cb < 128) trace(405 + (cb >> 4));
-    if (cb >= my0 && cb + 32 <= my1) {
-      // The whole chunk is this CTA's: park it in its slot of the gather area.
+    const int nv = min(32, V - cb);  // real tokens in this chunk
+    if (cb >= my0 && cb + nv <= my1) {
+      // Every real token of the chunk is this CTA's: park them in its slot
+      // of the gather area.
       float* o = own + static_cast<size_t>(cb - my0) * kTileP;
+      if (nv == 32) {
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) o[jj * kTileP] = __uint_as_float(r[jj]);
-    } else if ((cb + 32 <= my0 || cb >= my1) && cb + 32 <= V) {
-      // The whole chunk is other CTAs': to this CTA's exchange slab.
+        for (int jj = 0; jj < 32; ++jj) o[jj * kTileP] = __uint_as_float(r[jj]);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj)
+          if (jj < nv) o[jj * kTileP] = __uint_as_float(r[jj]);
+      }
+    } else if (cb + nv <= my0 || cb >= my1) {
+      // Every real token of the chunk is other CTAs': to this CTA's slab.
       float* m = mine + static_cast<size_t>(cb) * kTileP + row;
+      if (nv == 32) {
 #pragma unroll
-      for (int jj = 0; jj < 32; ++jj) __stcg(m + jj * kTileP, __uint_as_float(r[jj]));
+        for (int jj = 0; jj < 32; ++jj) __stcg(m + jj * kTileP, __uint_as_float(r[jj]));
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj)
+          if (jj < nv) __stcg(m + jj * kTileP, __uint_as_float(r[jj]));
+      }
     } else {
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
@@ -721,13 +735,16 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
           for (int jj = 0; jj < 32; ++jj) v[jj] += sq[jj * kTileP];
         }
       } else {
+        // The run's last, partial chunk: tokens past it read as 0 (those
+        // lanes of the staging tile are not emitted).
 #pragma unroll
-        for (int jj = 0; jj < 32; ++jj) v[jj] = s0[static_cast<size_t>(min(jj, lim)) * kTileP];
+        for (int jj = 0; jj < 32; ++jj) v[jj] = jj <= lim ? s0[jj * kTileP] : 0.f;
 #pragma unroll 1
         for (int q = 1; q < S; ++q) {
           const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
 #pragma unroll
-          for (int jj = 0; jj < 32; ++jj) v[jj] += sq[static_cast<size_t>(min(jj, lim)) * kTileP];
+          for (int jj = 0; jj < 32; ++jj)
+            if (jj <= lim) v[jj] += sq[jj * kTileP];
         }
       }
 #pragma unroll
@@ -738,11 +755,16 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
     }
   }
 
-  // 4. The last CTA of the tile to finish resets its counters.
+  // 4. The last CTA of the tile to finish resets its counters. Relaxed: each
+  //    CTA's poll of the first counter and its gather have completed before
+  //    its increment (program order, bar.sync), so the reset cannot reach a
+  //    wait still in progress, and the next launch sees it across the kernel
+  //    boundary. No release is needed, so the output stores need not drain
+  //    first.
   named_bar_sync(1, kEpiThreads);
   if (tid == 0) {
     trace(1013);
-    const uint32_t old = atom_add_acqrel_gpu(ctr + 1, 1u);
+    const uint32_t old = atom_add_relaxed_gpu(ctr + 1, 1u);
     if (old == static_cast<uint32_t>(S) - 1u) {
       ctr[0] = 0u;
       ctr[1] = 0u;
