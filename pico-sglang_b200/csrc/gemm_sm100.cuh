@@ -637,6 +637,10 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
       if (nv == 32) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) o[jj * kTileP] = __uint_as_float(r[jj]);
+      } else if (nv <= 8) {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)
+          if (jj < nv) o[jj * kTileP] = __uint_as_float(r[jj]);
       } else {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj)
@@ -648,6 +652,10 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
       if (nv == 32) {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj) __stcg(m + jj * kTileP, __uint_as_float(r[jj]));
+      } else if (nv <= 8) {
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)
+          if (jj < nv) __stcg(m + jj * kTileP, __uint_as_float(r[jj]));
       } else {
 #pragma unroll
         for (int jj = 0; jj < 32; ++jj)
@@ -733,6 +741,22 @@ __device__ __forceinline__ bool split_reduce_tile(const GemmShape& g, const Seg&
           const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
 #pragma unroll
           for (int jj = 0; jj < 32; ++jj) v[jj] += sq[jj * kTileP];
+        }
+      } else if (lim < 8) {
+        // A short run (decode batches of up to 8 tokens): 8 columns at most;
+        // tokens past it read as 0 (those lanes of the staging tile are not
+        // emitted).
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) v[jj] = 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)
+          if (jj <= lim) v[jj] = s0[jj * kTileP];
+#pragma unroll 1
+        for (int q = 1; q < S; ++q) {
+          const float* sq = base + (static_cast<size_t>(q) * n_mine + c0) * kTileP;
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj)
+            if (jj <= lim) v[jj] += sq[jj * kTileP];
         }
       } else {
         // The run's last, partial chunk: tokens past it read as 0 (those
