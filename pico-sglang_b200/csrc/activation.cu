@@ -40,6 +40,9 @@ __device__ __forceinline__ void act_piece(const E* g, const E* u, E* o) {
 template <typename E, int VEC>
 __global__ void __launch_bounds__(kActThreads) silu_and_mul_kernel(const E* __restrict__ in, E* __restrict__ out,
                                                                    int T, int I) {
+  // The next kernel may become resident and prefetch its weights; it reads
+  // this kernel's output only after its own wait.
+  if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
   const long long per_row = I / VEC;
   const long long total = static_cast<long long>(T) * per_row;

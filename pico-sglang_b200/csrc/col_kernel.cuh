@@ -243,6 +243,252 @@ __global__ void __launch_bounds__(kGemmThreads, gemm_ctas_per_sm(BN))
   if (threadIdx.x == 0) trace(1001);
 }
 
+// Prefill shapes on CTA pairs (cta_group::2). A cluster of two CTAs computes
+// one 256-token x 256-column output tile with tcgen05.mma.cta_group::2
+// (M = 256, N = 256). CTA r of the pair holds tokens [128 r, 128 r + 128) of
+// the tile (the MMA's A rows) and weight rows [128 r, 128 r + 128) of its 256
+// (the B half; in gated mode the gate rows in the even CTA and the up rows of
+// the same 128 features in the odd one). Each CTA loads 32 KB per k-block for
+// the same MMA work per SM for which a single CTA's 128 x 256 tile loads
+// 48 KB; at these shapes the main loop is bound by L2-to-SM bandwidth.
+//
+// The even CTA (rank 0) issues every MMA. Both CTAs' TMA loads count their
+// bytes on its full barriers, which only it arms (expect_tx of both halves).
+// Its commits arrive on the empty and accumulator-full barriers of both CTAs.
+// Each CTA's epilogue reads its own TMEM (its 128 token rows x 256 columns)
+// through the policy's nonswap_tile and then arrives on the even CTA's
+// accumulator-empty barrier (two arrivals per phase). Tiles are dealt to the
+// pairs round-robin, tokens fastest, so consecutive pairs share weight
+// columns in L2. Every wait is bounded.
+constexpr int kPairStages = 6;
+
+template <typename IO, typename Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    col_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                         GemmShape g, const __grid_constant__ Epi epi) {
+  using L = GemmSmem<kTileP, kPairStages, Epi::kSmemBytes>;
+  extern __shared__ uint8_t smem_raw[];
+  GemmCtl c = gemm_carve_smem<kTileP, kPairStages, Epi::kSmemBytes>(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(cluster_id_x());
+  const int npairs = static_cast<int>(cluster_count_x());
+  const int MT = (g.T + 2 * kTileP - 1) / (2 * kTileP);
+  const int PT = MT * g.q_tiles;
+
+  if (threadIdx.x == 0) {
+    trace(1000);
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+    for (int i = 0; i < kPairStages; ++i) {
+      mbar_init(&c.full[i], 1);
+      mbar_init(&c.empty[i], 1);
+    }
+    mbar_init(&c.acc_full[0], 1);
+    mbar_init(&c.acc_full[1], 1);
+    mbar_init(&c.acc_empty[0], 2);
+    mbar_init(&c.acc_empty[1], 2);
+    mbar_init(c.drain, 1);
+    mbar_init(c.xchg, 1);
+    *c.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(c.tmem_base, 4 * kTileP);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers exist before any remote arrival or byte count
+  tc_fence_after();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer, both CTAs.
+      const uint64_t hx = l2_policy_evict_last();
+      const uint64_t hw = l2_policy_evict_first();
+      const uint32_t full0 = dsmem_addr(&c.full[0], 0);
+      pdl_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = pair; ok && u < PT; u += npairs) {
+        const int mt = u % MT, nt = u / MT;
+        const int xrow = mt * 2 * kTileP + static_cast<int>(rank) * kTileP;
+        const int wrow = g.glu ? (rank == 0 ? nt * kTileP : g.N + nt * kTileP)
+                               : nt * 2 * kTileP + static_cast<int>(rank) * kTileP;
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!mbar_wait(&c.empty[stage], phase ^ 1u, g.wait_ns, c.abort)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&c.full[stage], 2u * L::kStageBytes);
+          const uint32_t fb = full0 + 8u * static_cast<uint32_t>(stage);
+          tma_load_2d_pair(&tm_x, fb, c.a + stage * L::kABytes, kb * kBlockK, xrow, hx);
+          tma_load_2d_pair(&tm_w, fb, c.b + stage * L::kBBytes, kb * kBlockK, wrow, hw);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // MMA issuer: the even CTA only.
+      const uint32_t idesc = umma_idesc_f16(2 * kTileP, 2 * kTileP, std::is_same<IO, __nv_bfloat16>::value);
+      const uint32_t tmem = *c.tmem_base;
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true, any = false;
+      for (int u = pair; ok && u < PT; u += npairs) {
+        if (!mbar_wait_cluster(&c.acc_empty[acc], acc_phase ^ 1u, g.wait_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * 2 * kTileP);
+        for (int kb = 0; kb < g.kblocks; ++kb) {
+          if (!mbar_wait(&c.full[stage], phase, g.wait_ns, c.abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128_kmajor(smem_u32(c.a + stage * L::kABytes));
+          const uint64_t db = umma_desc_sw128_kmajor(smem_u32(c.b + stage * L::kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k)
+            umma_f16_ss_pair(d, da + static_cast<uint64_t>(2 * k), db + static_cast<uint64_t>(2 * k), idesc,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_pair_both(&c.empty[stage]);
+          any = true;
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_both(&c.acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+        if (any) {
+          // No MMA may still read shared memory or write TMEM when the pair
+          // leaves: a commit tracks every earlier MMA of this thread.
+          umma_commit_pair_local(c.drain);
+          (void)mbar_wait(c.drain, 0u, 10000000ull, nullptr);
+        }
+      }
+    }
+  } else {
+    // Epilogue, both CTAs: this CTA's 128 token rows of each tile.
+    pdl_wait();
+    epi.template prepare<false>(g, c);
+    const uint32_t tmem = *c.tmem_base;
+    const uint32_t empty0 = dsmem_addr(&c.acc_empty[0], 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = pair; u < PT; u += npairs) {
+      if (!mbar_wait_cluster(&c.acc_full[acc], acc_phase, g.wait_ns)) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+        break;
+      }
+      tc_fence_after();
+      const int mt = u % MT, nt = u / MT;
+      epi.template nonswap_tile<2 * kTileP>(g, tmem, acc, 2 * mt + static_cast<int>(rank), nt);
+      tc_fence_before();
+      named_bar_sync(1, kEpiThreads);
+      if (epi_tid() == 0) mbar_arrive_cluster(empty0 + 8u * static_cast<uint32_t>(acc));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no commit or arrival from the peer is still on its way
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(*c.tmem_base, 4 * kTileP);
+  }
+  if (threadIdx.x == 0) trace(1001);
+}
+
+// Launch the pair kernel for a prefill plan (p.pair). Same arguments as
+// launch_col.
+template <typename IO, typename Epi>
+int launch_col_pair(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
+                    const ColScratch& sc, cudaStream_t stream, const Epi& epi) {
+  using L = GemmSmem<kTileP, kPairStages, Epi::kSmemBytes>;
+  static_assert(L::kBytes <= 232448, "shared memory budget");
+  auto kern = col_gemm_pair_kernel<IO, Epi>;
+  if (L::kBytes > dev.max_smem_optin)
+    return set_error(PGB_ERR_UNSUPPORTED, "kernel needs %d B shared memory, device allows %d", L::kBytes,
+                     dev.max_smem_optin);
+  PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
+  CUtensorMap tm_x, tm_w;
+  int rc = make_tmap_2d_16bit(&tm_x, x, K, T, static_cast<uint64_t>(K) * 2, kBlockK, kTileP, kBf16);
+  if (rc) return rc;
+  rc = make_tmap_2d_16bit(&tm_w, w, K, Epi::kGlu ? 2 * N : N, static_cast<uint64_t>(K) * 2, kBlockK, kTileP, kBf16);
+  if (rc) return rc;
+
+  GemmShape g{};
+  g.T = T;
+  g.N = N;
+  g.K = K;
+  g.kblocks = p.kblocks;
+  g.p_tiles = p.p_tiles;
+  g.q_tiles = p.q_tiles;
+  g.tiles = p.tiles;
+  g.dp_rounds = p.dp_rounds;
+  g.split_first = p.tiles;
+  g.grid = p.grid;
+  g.split_ctas = 0;
+  g.nsplit = 1;
+  g.status = sc.status;
+  g.ctr = sc.ctr;
+  g.xchg = sc.xchg;
+  g.wait_ns = 2000000000ull;
+  g.glu = Epi::kGlu ? 1 : 0;
+
+  const int pair_tiles = ((T + 2 * kTileP - 1) / (2 * kTileP)) * p.q_tiles;
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute cl{};
+  cl.id = cudaLaunchAttributeClusterDimension;
+  cl.val.clusterDim.x = 2;
+  cl.val.clusterDim.y = 1;
+  cl.val.clusterDim.z = 1;
+  cfg.attrs = &cl;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2 * (dev.sm_count / 2));
+  int clusters = 0;
+  PGB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+  if (clusters < 1) return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: no CTA pair fits an SM pair");
+  clusters = std::min(clusters, std::min(pair_tiles, dev.sm_count / 2));
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
+  return launch_ex(cfg, /*cooperative=*/false, 2, kern, tm_x, tm_w, g, epi);
+}
+
 // Launch one column kernel. N is the output width g.N; the weight has N rows,
 // or 2N ([gate; up]) for a gated policy. sc is the split-K scratch (a column
 // workspace, col_scratch(), or a communicator's device-local area).
@@ -310,6 +556,7 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
 template <typename IO, typename Epi>
 int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
                  const ColScratch& sc, cudaStream_t stream, const Epi& epi) {
+  if (!p.swap && p.pair) return launch_col_pair<IO>(p, dev, x, w, T, N, K, sc, stream, epi);
   if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, T, N, K, sc, stream, epi);
   switch (p.bn) {
     case 32: return launch_col<IO, 32, true>(p, dev, x, w, T, N, K, sc, stream, epi);

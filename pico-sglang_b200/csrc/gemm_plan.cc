@@ -65,6 +65,9 @@ GemmPlan plan_gemm(int T, int N, int K, int sms, size_t max_exchange_bytes) {
   p.exchange_bytes = 0;
   p.counter_bytes = 0;
   p.est_us = p.dp_rounds * p.kblocks * t_kb;
+  // Prefill: the column kernel runs these tiles on CTA pairs (256 x 256 per
+  // pair, cta_group::2), which load a third less per MMA than one CTA.
+  p.pair = !p.swap;
   if (!p.swap) return p;
 
   // Short reductions at wide batches (T > 64, at most 32 k-blocks: the

@@ -22,6 +22,7 @@ struct GemmPlan {
   size_t exchange_bytes;  // split-K exchange area (0 without split tiles)
   size_t counter_bytes;   // per-split-tile counters (aligned)
   double est_us;  // cost-model estimate of the chosen decomposition
+  bool pair;      // prefill orientation on CTA pairs (cta_group::2, 256 x 256 tiles; column kernel)
 };
 
 // Plan y[T, N] = x[T, K] . W[N, K]^T on a device with `sms` SMs.

@@ -19,6 +19,9 @@ __global__ void __launch_bounds__(kNormThreads) fused_add_rmsnorm_kernel(IO* x, 
                                                                          const IO* w, float eps,
                                                                          int width) {
   __shared__ float red[32];
+  // The next kernel (a GEMM) may become resident now and prefetch its
+  // weights; it reads this kernel's outputs only after its own wait.
+  if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
   const int t = blockIdx.x;
   const int nvec = width >> 3;
@@ -58,6 +61,7 @@ template <typename IO>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const IO* x, const IO* w, float eps,
                                                                IO* out, int width) {
   __shared__ float red[32];
+  if (threadIdx.x == 0) pdl_launch_dependents();  // as in fused_add_rmsnorm_kernel
   pdl_wait();
   const int t = blockIdx.x;
   const int nvec = width >> 3;

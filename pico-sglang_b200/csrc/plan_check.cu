@@ -128,8 +128,8 @@ extern "C" int pgb_describe_plan(int T, int N, int K, int sms, int fused_row, in
   const GemmPlan p = plan_for(T, N, K, sms, fused_row);
   snprintf(out, out_bytes,
            "swap=%d bn=%d tiles=%d kblocks=%d grid=%d dp_rounds=%d split_first=%d split_ctas=%d nsplit=%d "
-           "exchange_bytes=%zu est_us=%.2f",
+           "exchange_bytes=%zu est_us=%.2f pair=%d",
            p.swap ? 1 : 0, p.bn, p.tiles, p.kblocks, p.grid, p.dp_rounds, p.split_first, p.split_ctas, p.nsplit,
-           p.exchange_bytes, p.est_us);
+           p.exchange_bytes, p.est_us, (p.pair && !fused_row) ? 1 : 0);
   return PGB_OK;
 }

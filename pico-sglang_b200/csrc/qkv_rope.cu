@@ -277,6 +277,9 @@ namespace {
 // thread per 8 features of a token.
 template <typename E>
 __global__ void __launch_bounds__(256) rope_store_kernel(const E* __restrict__ qkv, int T, RopeStore<E> rs) {
+  // The next kernel may become resident and prefetch its weights; it reads
+  // this kernel's outputs only after its own wait.
+  if (threadIdx.x == 0) pdl_launch_dependents();
   pdl_wait();
   const int N = (rs.nq + 2 * rs.nkv) * rs.hd;
   const int per_row = N / 8, half = rs.rd >> 1;
