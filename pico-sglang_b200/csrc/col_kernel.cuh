@@ -428,6 +428,282 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) trace(1001);
 }
 
+// Decode batches of 129-256 tokens on CTA pairs (swap orientation). A pair
+// tile is 256 weight rows x the batch's 256 token columns: CTA r holds weight
+// rows [128 r, 128 r + 128) of it (its own 128-row tile p = 2 pt + r) and
+// tokens [128 r, 128 r + 128) of the batch (the B half). Each CTA loads 32 KB
+// per k-block where a single CTA of the same work loads 48 KB (the batch's
+// 32 KB activation tile dominated). The decomposition (GemmShape) counts
+// pairs: whole pair tiles round-robin, then split pair tiles over S pairs.
+// Each CTA's accumulator is an ordinary 128-row swap tile, so the epilogue
+// and the split-K reduce-scatter run per CTA as in col_gemm_kernel, with the
+// split partners being the same-rank CTAs of the tile's S pairs (exchange
+// halves 2 u + r). Split partners wait for each other: all pairs of a launch
+// must be resident together, which the launcher checks against the occupancy
+// of a cluster launch.
+template <typename IO, typename Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    col_gemm_pair_swap_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                              GemmShape g, const __grid_constant__ Epi epi) {
+  constexpr int BN = 2 * kTileP;  // tokens per pair tile
+  using L = GemmSmem<kTileP, kPairStages, Epi::kSmemBytes>;
+  extern __shared__ uint8_t smem_raw[];
+  GemmCtl c = gemm_carve_smem<kTileP, kPairStages, Epi::kSmemBytes>(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(cluster_id_x());
+
+  if (threadIdx.x == 0) {
+    trace(1000);
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+    for (int i = 0; i < kPairStages; ++i) {
+      mbar_init(&c.full[i], 1);
+      mbar_init(&c.empty[i], 1);
+    }
+    mbar_init(&c.acc_full[0], 1);
+    mbar_init(&c.acc_full[1], 1);
+    mbar_init(&c.acc_empty[0], 2);
+    mbar_init(&c.acc_empty[1], 2);
+    mbar_init(c.drain, 1);
+    mbar_init(c.xchg, 1);
+    *c.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(c.tmem_base, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers exist before any remote arrival or byte count
+  tc_fence_after();
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // Producer, both CTAs: this CTA's weight rows and token half, bytes
+      // counted on the even CTA's full barriers.
+      const uint64_t hw = l2_policy_evict_first();
+      const uint64_t hx = l2_policy_evict_last();
+      const uint32_t full0 = dsmem_addr(&c.full[0], 0);
+      pdl_wait();
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      SegIter it(g, pair);
+      Seg tc;
+      while (ok && it.next(g, tc)) {
+        Seg mine = tc;
+        mine.p = 2 * tc.p + static_cast<int>(rank);
+        for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
+          if (!mbar_wait(&c.empty[stage], phase ^ 1u, g.wait_ns, c.abort)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&c.full[stage], 2u * L::kStageBytes);
+          const uint32_t fb = full0 + 8u * static_cast<uint32_t>(stage);
+          uint8_t* a = c.a + stage * L::kABytes;
+          if (!g.glu) {
+            tma_load_2d_pair(&tm_w, fb, a, kb * kBlockK, mine.p * kTileP, hw);
+          } else {
+            const int r0 = mine.p * (kTileP / 2);
+            tma_load_2d_pair(&tm_w, fb, a, kb * kBlockK, r0, hw);
+            tma_load_2d_pair(&tm_w, fb, a + (kTileP / 2) * kBlockK * 2, kb * kBlockK, g.N + r0, hw);
+          }
+          tma_load_2d_pair(&tm_x, fb, c.b + stage * L::kBBytes, kb * kBlockK, static_cast<int>(rank) * kTileP, hx);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // MMA issuer: the even CTA only.
+      const uint32_t idesc = umma_idesc_f16(2 * kTileP, BN, std::is_same<IO, __nv_bfloat16>::value);
+      const uint32_t tmem = *c.tmem_base;
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true, any = false;
+      SegIter it(g, pair);
+      Seg tc;
+      while (ok && it.next(g, tc)) {
+        if (!mbar_wait_cluster(&c.acc_empty[acc], acc_phase ^ 1u, g.wait_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * BN);
+        for (int kb = tc.kb0; kb < tc.kb1; ++kb) {
+          if (!mbar_wait(&c.full[stage], phase, g.wait_ns, c.abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128_kmajor(smem_u32(c.a + stage * L::kABytes));
+          const uint64_t db = umma_desc_sw128_kmajor(smem_u32(c.b + stage * L::kBBytes));
+#pragma unroll
+          for (int k = 0; k < kBlockK / 16; ++k)
+            umma_f16_ss_pair(d, da + static_cast<uint64_t>(2 * k), db + static_cast<uint64_t>(2 * k), idesc,
+                             (kb > tc.kb0 || k > 0) ? 1u : 0u);
+          umma_commit_pair_both(&c.empty[stage]);
+          any = true;
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_both(&c.acc_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+        if (any) {
+          umma_commit_pair_local(c.drain);
+          (void)mbar_wait(c.drain, 0u, 10000000ull, nullptr);
+        }
+      }
+    }
+  } else {
+    // Epilogue, both CTAs: this CTA's 128-row tile of each segment.
+    pdl_wait();
+    epi.template prepare<true>(g, c);
+    const uint32_t tmem = *c.tmem_base;
+    const uint32_t empty0 = dsmem_addr(&c.acc_empty[0], 0);
+    const int row = epi_row();
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    SegIter it(g, pair);
+    Seg tc;
+    while (it.next(g, tc)) {
+      if (!mbar_wait_cluster(&c.acc_full[acc], acc_phase, g.wait_ns)) {
+        record_error(g.status, kDevTimeoutPipeline);
+        *reinterpret_cast<volatile int*>(c.abort) = 1;
+        break;
+      }
+      tc_fence_after();
+      Seg sv = tc;
+      sv.p = 2 * tc.p + static_cast<int>(rank);
+      if (tc.nctb > 1) {
+        // Exchange half 2 u + r of split pair tile u.
+        sv.tile = g.split_first + 2 * (tc.tile - g.split_first) + static_cast<int>(rank);
+        split_reduce_tile<BN>(g, sv, c, tmem, acc, epi.row_bias(g, sv.p, row),
+                              [&](const float* v, int t0, int t_lo, int t_hi) {
+                                epi.swap_chunk(g, c, v, sv.p, t0, t_lo, t_hi);
+                              });
+      } else {
+        const float b = epi.row_bias(g, sv.p, row);
+#pragma unroll 1
+        for (int col = 0; col < BN; col += 32) {
+          float v[32];
+          epi_load_chunk<BN>(tmem, acc, col, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += b;
+          epi.swap_chunk(g, c, v, sv.p, col, 0, g.T);
+        }
+      }
+      tc_fence_before();
+      named_bar_sync(1, kEpiThreads);
+      if (epi_tid() == 0) mbar_arrive_cluster(empty0 + 8u * static_cast<uint32_t>(acc));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no commit or arrival from the peer is still on its way
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(*c.tmem_base, 2 * BN);
+  }
+  if (threadIdx.x == 0) trace(1001);
+}
+
+// Launch the decode pair kernel for a swap plan with p.pair (counted in
+// pairs). Same arguments as launch_col.
+template <typename IO, typename Epi>
+int launch_col_pair_swap(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
+                         const ColScratch& sc, cudaStream_t stream, const Epi& epi) {
+  using L = GemmSmem<kTileP, kPairStages, Epi::kSmemBytes>;
+  static_assert(L::kBytes <= 232448, "shared memory budget");
+  auto kern = col_gemm_pair_swap_kernel<IO, Epi>;
+  if (L::kBytes > dev.max_smem_optin)
+    return set_error(PGB_ERR_UNSUPPORTED, "kernel needs %d B shared memory, device allows %d", L::kBytes,
+                     dev.max_smem_optin);
+  PGB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+  if (p.nsplit > 1 && split_recv_bytes(2 * kTileP, p.nsplit) > static_cast<size_t>(kPairStages) * L::kStageBytes)
+    return set_error(PGB_ERR_STATE, "col_gemm: split of %d does not fit the pipeline ring", p.nsplit);
+  if (p.exchange_bytes > sc.xchg_bytes)
+    return set_error(PGB_ERR_INVALID, "col_gemm: split exchange of %zu bytes, scratch holds %zu", p.exchange_bytes,
+                     sc.xchg_bytes);
+  if (p.counter_bytes > sc.ctr_bytes)
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d split tiles exceed the counter region",
+                     2 * (p.tiles - p.split_first));
+
+  constexpr bool kBf16 = std::is_same<IO, __nv_bfloat16>::value;
+  CUtensorMap tm_x, tm_w;
+  int rc = make_tmap_2d_16bit(&tm_x, x, K, T, static_cast<uint64_t>(K) * 2, kBlockK, kTileP, kBf16);
+  if (rc) return rc;
+  constexpr int kWRows = kTileP / (Epi::kGlu ? 2 : 1);
+  rc = make_tmap_2d_16bit(&tm_w, w, K, Epi::kGlu ? 2 * N : N, static_cast<uint64_t>(K) * 2, kBlockK, kWRows, kBf16);
+  if (rc) return rc;
+
+  GemmShape g{};
+  g.T = T;
+  g.N = N;
+  g.K = K;
+  g.kblocks = p.kblocks;
+  g.p_tiles = p.p_tiles;
+  g.q_tiles = p.q_tiles;
+  g.tiles = p.tiles;
+  g.dp_rounds = p.dp_rounds;
+  g.split_first = p.split_first;
+  g.grid = p.grid;
+  g.split_ctas = p.split_ctas;
+  g.nsplit = p.nsplit;
+  g.status = sc.status;
+  g.ctr = sc.ctr;
+  g.xchg = sc.xchg;
+  g.wait_ns = 2000000000ull;
+  g.glu = Epi::kGlu ? 1 : 0;
+
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute cl{};
+  cl.id = cudaLaunchAttributeClusterDimension;
+  cl.val.clusterDim.x = 2;
+  cl.val.clusterDim.y = 1;
+  cl.val.clusterDim.z = 1;
+  cfg.attrs = &cl;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2 * p.grid);
+  int clusters = 0;
+  PGB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+  // Split partners spin on each other: every pair of the launch must fit at once.
+  if (clusters < p.grid)
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d CTA pairs planned, %d fit the device", p.grid, clusters);
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
+  return launch_ex(cfg, /*cooperative=*/false, 2, kern, tm_w, tm_x, g, epi);
+}
+
 // Launch the pair kernel for a prefill plan (p.pair). Same arguments as
 // launch_col.
 template <typename IO, typename Epi>
@@ -557,6 +833,7 @@ template <typename IO, typename Epi>
 int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
                  const ColScratch& sc, cudaStream_t stream, const Epi& epi) {
   if (!p.swap && p.pair) return launch_col_pair<IO>(p, dev, x, w, T, N, K, sc, stream, epi);
+  if (p.swap && p.pair) return launch_col_pair_swap<IO>(p, dev, x, w, T, N, K, sc, stream, epi);
   if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, T, N, K, sc, stream, epi);
   switch (p.bn) {
     case 32: return launch_col<IO, 32, true>(p, dev, x, w, T, N, K, sc, stream, epi);

@@ -31,7 +31,7 @@ int col_gemm_on_scratch(const void* x, const void* w, const void* bias, void* y,
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc) return rc;
-  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, sc.xchg_bytes);
+  const GemmPlan p = plan_gemm_col(T, N, K, dev.sm_count, sc.xchg_bytes);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == PGB_BF16)
     return dispatch_col<__nv_bfloat16>(p, dev, x, w, T, N, K, sc, s,
@@ -47,7 +47,7 @@ int col_gemm_on_scratch(const void* x, const void* w, const void* bias, void* y,
 
 extern "C" size_t pgb_col_gemm_workspace_size(int T, int N, int K) {
   if (T <= 0 || N <= 0 || K <= 0) return pgb::kWsHeaderBytes;
-  const pgb::GemmPlan p = pgb::plan_gemm(T, N, K, pgb::sm_count_or_default(), SIZE_MAX);
+  const pgb::GemmPlan p = pgb::plan_gemm_col(T, N, K, pgb::sm_count_or_default(), SIZE_MAX);
   return pgb::col_workspace_bytes(p);
 }
 
@@ -77,7 +77,7 @@ extern "C" int pgb_col_gemm(const void* x, const void* w, const void* bias, void
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc) return rc;
-  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, SIZE_MAX);
+  const GemmPlan p = plan_gemm_col(T, N, K, dev.sm_count, SIZE_MAX);
   const size_t need = col_workspace_bytes(p);
   if (workspace_bytes < need)
     return set_error(PGB_ERR_INVALID, "col_gemm: workspace of %zu bytes, %zu needed", workspace_bytes,
@@ -111,7 +111,7 @@ extern "C" size_t pgb_gate_up_silu_workspace_size(int T, int I, int K, int dtype
   using namespace pgb;
   if (T <= 0 || I <= 0 || K <= 0) return kWsHeaderBytes;
   if (dtype == PGB_F32) return kWsHeaderBytes + kWsCounterBytes + f32_gate_up_bytes(T, I);
-  const GemmPlan p = plan_gemm(T, 2 * I, K, sm_count_or_default(), SIZE_MAX);
+  const GemmPlan p = plan_gemm_col(T, 2 * I, K, sm_count_or_default(), SIZE_MAX);
   return col_workspace_bytes(p);
 }
 
@@ -147,7 +147,7 @@ extern "C" int pgb_gate_up_silu(const void* x, const void* w, const void* bias, 
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc) return rc;
-  const GemmPlan p = plan_gemm(T, 2 * I, K, dev.sm_count, SIZE_MAX);
+  const GemmPlan p = plan_gemm_col(T, 2 * I, K, dev.sm_count, SIZE_MAX);
   const size_t need = col_workspace_bytes(p);
   if (workspace_bytes < need)
     return set_error(PGB_ERR_INVALID, "gate_up_silu: workspace of %zu bytes, %zu needed", workspace_bytes,
@@ -242,7 +242,7 @@ extern "C" int pgb_col_gemm_noalloc(const void* x, const void* w, const void* bi
   DeviceInfo dev;
   int rc = current_device_info(&dev);
   if (rc) return rc;
-  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, SIZE_MAX);
+  const GemmPlan p = plan_gemm_col(T, N, K, dev.sm_count, SIZE_MAX);
   const size_t need = col_workspace_bytes(p);
   if (need > PGB_NOALLOC_SCRATCH_BYTES)
     return set_error(PGB_ERR_INVALID,

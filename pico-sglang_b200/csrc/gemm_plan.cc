@@ -115,4 +115,51 @@ GemmPlan plan_gemm(int T, int N, int K, int sms, size_t max_exchange_bytes) {
   return best;
 }
 
+GemmPlan plan_gemm_col(int T, int N, int K, int sms, size_t max_exchange_bytes) {
+  const GemmPlan base = plan_gemm(T, N, K, sms, max_exchange_bytes);
+  if (!base.swap || base.bn != 256 || base.q_tiles != 1 || N < 512) return base;
+  // Pairs are the unit of work: a 256-row weight tile per pair, its MMA
+  // bound at one 256 x 256 x 64 k-block per 0.36 us (each CTA loads 32 KB
+  // per k-block, which L2 sustains), the split tail as for single CTAs.
+  constexpr double kKbPairUs = 0.36;
+  const int units = sms / 2;
+  GemmPlan p = base;
+  p.pair = true;
+  p.bn = 256;
+  p.p_tiles = div_up(N, 256);
+  p.q_tiles = 1;
+  p.tiles = p.p_tiles;
+  p.grid = std::min(units, p.tiles);
+  p.dp_rounds = div_up(p.tiles, p.grid);
+  p.split_first = p.tiles;
+  p.split_ctas = 0;
+  p.nsplit = 1;
+  p.exchange_bytes = 0;
+  p.counter_bytes = 0;
+  p.est_us = p.dp_rounds * p.kblocks * kKbPairUs;
+  const int full = p.tiles / units;
+  const int rem = p.tiles - full * units;
+  GemmPlan best = p;
+  if (rem > 0) {
+    const int s_max = std::min({kMaxSplit, units / rem, p.kblocks});
+    for (int S = 2; S <= s_max; ++S) {
+      GemmPlan q = p;
+      q.dp_rounds = full;
+      q.split_first = full * units;
+      q.grid = full > 0 ? units : rem * S;
+      q.split_ctas = rem * S;
+      q.nsplit = S;
+      q.exchange_bytes = static_cast<size_t>(rem) * 2u * S * 128u * 256u * 4u;
+      q.counter_bytes = (static_cast<size_t>(rem) * 2u * 8u + 255u) / 256u * 256u;
+      if (q.exchange_bytes > max_exchange_bytes) continue;
+      const double moved = 2.0 * (S - 1.0) / S * 128.0 * std::min(T, 256) * 4.0;
+      q.est_us = full * q.kblocks * kKbPairUs + div_up(q.kblocks, S) * kKbPairUs + kSplitFixedUs +
+                 moved / kExchangeBytesPerUs;
+      if (q.est_us < best.est_us) best = q;
+    }
+  }
+  // The single-CTA plan stays when the pairs cannot cover the SMs as well.
+  return best.est_us <= base.est_us ? best : base;
+}
+
 }  // namespace pgb

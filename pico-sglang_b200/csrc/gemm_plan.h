@@ -22,13 +22,21 @@ struct GemmPlan {
   size_t exchange_bytes;  // split-K exchange area (0 without split tiles)
   size_t counter_bytes;   // per-split-tile counters (aligned)
   double est_us;  // cost-model estimate of the chosen decomposition
-  bool pair;      // prefill orientation on CTA pairs (cta_group::2, 256 x 256 tiles; column kernel)
+  bool pair;      // CTA pairs (cta_group::2, column kernels only). Prefill: 256 x 256 tiles, the
+                  // other fields describe single-CTA tiles. Decode (swap): the fields count pairs
+                  // and 256-row weight tiles; each split tile has two exchange halves.
 };
 
 // Plan y[T, N] = x[T, K] . W[N, K]^T on a device with `sms` SMs.
 // max_exchange_bytes caps the split-K exchange area (SIZE_MAX: no cap).
 // The cheapest candidate under a measured-rate cost model is returned.
 GemmPlan plan_gemm(int T, int N, int K, int sms, size_t max_exchange_bytes);
+
+// The plan the column kernels run: plan_gemm's, or for 256-token decode
+// batches the same decomposition over CTA pairs (256 weight rows per pair
+// tile, half the batch's tokens per CTA), which the row-parallel kernels do
+// not use.
+GemmPlan plan_gemm_col(int T, int N, int K, int sms, size_t max_exchange_bytes);
 
 // Scratch layout used by the column GEMM: [status word | split-tile counters
 // | exchange area]. The counter region has one size and place for every

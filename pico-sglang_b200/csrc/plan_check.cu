@@ -16,7 +16,7 @@
 
 namespace {
 pgb::GemmPlan plan_for(int T, int N, int K, int sms, int fused_row) {
-  return pgb::plan_gemm(T, N, K, sms, fused_row ? pgb::kSplitScratchBytes : SIZE_MAX);
+  return fused_row ? pgb::plan_gemm(T, N, K, sms, pgb::kSplitScratchBytes) : pgb::plan_gemm_col(T, N, K, sms, SIZE_MAX);
 }
 }  // namespace
 

@@ -388,7 +388,7 @@ extern "C" size_t pgb_qkv_rope_store_workspace_size(int T, int num_q_heads, int 
   const int N = (num_q_heads + 2 * num_kv_heads) * head_dim;
   if (T <= 0 || N <= 0 || K <= 0) return kWsHeaderBytes + kWsCounterBytes;
   if (dtype == PGB_F32) return kWsHeaderBytes + kWsCounterBytes + f32_qkv_bytes(T, N);
-  const GemmPlan p = plan_gemm(T, N, K, sm_count_or_148(), SIZE_MAX);
+  const GemmPlan p = plan_gemm_col(T, N, K, sm_count_or_148(), SIZE_MAX);
   if (!rope_in_epilogue(head_dim)) return wide_qkv_offset(p) + f32_qkv_bytes(T, N) / 2;
   return col_workspace_bytes(p);
 }
@@ -434,7 +434,7 @@ extern "C" int pgb_qkv_rope_store(const void* x, const void* w, const void* bias
   DeviceInfo dev;
   rc = current_device_info(&dev);
   if (rc) return rc;
-  const GemmPlan p = plan_gemm(T, N, K, dev.sm_count, SIZE_MAX);
+  const GemmPlan p = plan_gemm_col(T, N, K, dev.sm_count, SIZE_MAX);
   const bool fused = rope_in_epilogue(hd);
   const size_t need = fused ? col_workspace_bytes(p) : wide_qkv_offset(p) + f32_qkv_bytes(T, N) / 2;
   if (workspace_bytes < need)
