@@ -114,15 +114,18 @@ PGB_API int pgb_comm_set_timeout_ns(pgb_comm* comm, uint64_t ns);
  * same. No reference counterpart. */
 PGB_API int pgb_comm_set_one_rank_path(pgb_comm* comm, int fused);
 
-/* Multi-rank decode row ops (T <= 256, 16-bit types): which exchange
+/* Multi-rank row ops (16-bit types): which exchange
  * pgb_row_gemm_allreduce_addnorm uses.
- *   PGB_XCHG_AUTO     the default: the grid-barrier kernel (one-shot or
- *                     two-shot rows by a cost model), measured fastest
+ *   PGB_XCHG_AUTO     the default: decode batches (T <= 256) on the
+ *                     grid-barrier kernel (one-shot or two-shot rows by a
+ *                     cost model); prefill batches (T > 256) as the column
+ *                     GEMM on CTA pairs, pgb_all_reduce over its output and
+ *                     pgb_fused_add_rmsnorm, measured faster there
  *   PGB_XCHG_ONESHOT  per-piece exchange kernel, every rank reduces every row
  *   PGB_XCHG_TWOSHOT  per-piece exchange kernel, reduce-scatter by feature
  *                     slices then all-gather of the reduced rows (needs
  *                     128 % world == 0 and N % 128 == 0, else one-shot)
- *   PGB_XCHG_BARRIER  the grid-barrier kernel (also serves prefill shapes)
+ *   PGB_XCHG_BARRIER  the grid-barrier kernel at every T (prefill included)
  *   PGB_XCHG_NVLS     partials stay in this GPU's multicast-bound memory; the
  *                     owner of each slice sums it over every GPU with
  *                     multimem.ld_reduce and broadcasts it with multimem.st

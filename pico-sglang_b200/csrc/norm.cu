@@ -12,7 +12,8 @@
 namespace pgb {
 
 constexpr int kNormThreads = 256;
-constexpr int kNormMaxVec = 8;  // width <= 256 * 64 = 16384
+constexpr int kNormMaxVec = 8;     // width <= 256 * 64 = 16384
+constexpr int kAddNormMaxVec = 4;  // fused_add_rmsnorm_kernel: width <= 256 * 32 = 8192 (wider rows: the rows kernel)
 
 template <typename IO>
 __global__ void __launch_bounds__(kNormThreads) fused_add_rmsnorm_kernel(IO* x, IO* residual,
@@ -25,10 +26,10 @@ __global__ void __launch_bounds__(kNormThreads) fused_add_rmsnorm_kernel(IO* x, 
   pdl_wait();
   const int t = blockIdx.x;
   const int nvec = width >> 3;
-  float s[kNormMaxVec][8];
+  float s[kAddNormMaxVec][8];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i) {
+  for (int i = 0; i < kAddNormMaxVec; ++i) {
     const int v = threadIdx.x + i * kNormThreads;
     if (v < nvec) {
       float a[8], r[8];
@@ -41,21 +42,80 @@ __global__ void __launch_bounds__(kNormThreads) fused_add_rmsnorm_kernel(IO* x, 
       }
     }
   }
-  const float rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
+  // The norm weights' loads are issued before the reduction, off its
+  // critical path; the residual is stored while the reduction runs.
+  float wv[kAddNormMaxVec][8];
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i) {
+  for (int i = 0; i < kAddNormMaxVec; ++i) {
     const int v = threadIdx.x + i * kNormThreads;
     if (v < nvec) {
-      const size_t off = static_cast<size_t>(t) * width + v * 8;
-      float wv[8], o[8];
-      load8<IO>(w + v * 8, wv);
-      store8<IO>(residual + off, s[i]);
+      load8<IO>(w + v * 8, wv[i]);
+      store8<IO>(residual + static_cast<size_t>(t) * width + v * 8, s[i]);
+    }
+  }
+  const float rcp = rsqrtf(block_sum(ss, red) / static_cast<float>(width) + eps);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = s[i][j] * rcp * wv[j];
-      store8<IO>(x + off, o);
+  for (int i = 0; i < kAddNormMaxVec; ++i) {
+    const int v = threadIdx.x + i * kNormThreads;
+    if (v < nvec) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = s[i][j] * rcp * wv[i][j];
+      store8<IO>(x + static_cast<size_t>(t) * width + v * 8, o);
     }
   }
 }
+
+// Long batches (prefill): one warp per row, 8 rows per CTA, rows strided over
+// a grid of at most 8 CTAs per SM. Pass 1 forms s = x + residual in f32 and
+// its sum of squares with many 16-byte loads in flight per lane; pass 2 reads
+// x and residual again (from L2, just fetched), forms the same s, stores the
+// rounded residual and s * rcp * w. The same arithmetic as
+// fused_add_rmsnorm_kernel except the order of the squares' sum.
+template <typename IO>
+__global__ void __launch_bounds__(kNormThreads) fused_add_rmsnorm_rows_kernel(IO* x, IO* residual, const IO* w,
+                                                                              float eps, int T, int width) {
+  if (threadIdx.x == 0) pdl_launch_dependents();  // as in fused_add_rmsnorm_kernel
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nvec = width >> 3;
+  for (int t = blockIdx.x * (kNormThreads / 32) + warp; t < T; t += gridDim.x * (kNormThreads / 32)) {
+    IO* xr = x + static_cast<size_t>(t) * width;
+    IO* rr = residual + static_cast<size_t>(t) * width;
+    float ss = 0.f;
+#pragma unroll 4
+    for (int v = lane; v < nvec; v += 32) {
+      float a[8], r[8];
+      load8<IO>(xr + v * 8, a);
+      load8<IO>(rr + v * 8, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float sj = a[j] + r[j];
+        ss += sj * sj;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rcp = rsqrtf(ss / static_cast<float>(width) + eps);
+#pragma unroll 4
+    for (int v = lane; v < nvec; v += 32) {
+      float a[8], r[8], wv[8], o[8];
+      load8<IO>(xr + v * 8, a);
+      load8<IO>(rr + v * 8, r);
+      load8<IO>(w + v * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        a[j] += r[j];
+        o[j] = a[j] * rcp * wv[j];
+      }
+      store8<IO>(rr + v * 8, a);
+      store8<IO>(xr + v * 8, o);
+    }
+  }
+}
+
+// Batches from this size up use fused_add_rmsnorm_rows_kernel.
+constexpr int kNormRowsKernelMinT = 1024;
 
 template <typename IO>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const IO* x, const IO* w, float eps,
@@ -126,6 +186,28 @@ extern "C" int pgb_fused_add_rmsnorm(void* x, void* residual, const void* w, flo
   int rc = check_norm_args("fused_add_rmsnorm", T, H, dtype, x, residual, w);
   if (rc || T == 0) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (T >= kNormRowsKernelMinT || H > kNormThreads * 8 * kAddNormMaxVec) {
+    DeviceInfo dev;
+    rc = current_device_info(&dev);
+    if (rc) return rc;
+    const int grid = std::min((T + kNormThreads / 32 - 1) / (kNormThreads / 32), 8 * dev.sm_count);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kNormThreads);
+    cfg.stream = s;
+    switch (dtype) {
+      case PGB_BF16:
+        return launch_ex(cfg, false, 1, fused_add_rmsnorm_rows_kernel<__nv_bfloat16>,
+                         static_cast<__nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(residual),
+                         static_cast<const __nv_bfloat16*>(w), eps, T, H);
+      case PGB_F16:
+        return launch_ex(cfg, false, 1, fused_add_rmsnorm_rows_kernel<__half>, static_cast<__half*>(x),
+                         static_cast<__half*>(residual), static_cast<const __half*>(w), eps, T, H);
+      default:
+        return launch_ex(cfg, false, 1, fused_add_rmsnorm_rows_kernel<float>, static_cast<float*>(x),
+                         static_cast<float*>(residual), static_cast<const float*>(w), eps, T, H);
+    }
+  }
   switch (dtype) {
     case PGB_BF16:
       rc = launch_norm(s, T, fused_add_rmsnorm_kernel<__nv_bfloat16>, 

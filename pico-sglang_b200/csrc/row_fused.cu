@@ -411,6 +411,34 @@ bool plan_rows(const pgb_comm* c, int rows, int width, int elem, RowSplit* rs) {
   return true;
 }
 
+// The row op as three launches: the column GEMM into out (on the
+// communicator's split scratch), the communicator's all-reduce over it, then
+// fused_add_rmsnorm in place. Used when the payload does not fit the
+// communicator's buffers (the reference then all-reduces in place,
+// csrc/src/pynccl.cu:127-135) and, by default, for prefill batches, where the
+// column GEMM runs on CTA pairs and beats the fused kernel's single-CTA tiles
+// by more than the exchange overlap gains.
+int row_unfused(pgb_comm* comm, const void* x_local, const void* w_local, const void* bias, void* residual,
+                const void* norm_w, float eps, void* out, int T, int N, int K_local, int dtype, void* stream) {
+  ColScratch sc;
+  sc.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
+  sc.ctr = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kCounters);
+  sc.ctr_bytes = kTileCounterBytes;
+  sc.xchg = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
+  sc.xchg_bytes = kSplitScratchBytes;
+  int rc = col_gemm_on_scratch(x_local, w_local, bias, out, T, N, K_local, dtype, sc, stream);
+  if (rc) return rc;
+  if (comm->world > 1) {
+    rc = pgb_all_reduce(comm, out, static_cast<size_t>(T) * N, dtype, PGB_OP_SUM, stream);
+    if (rc) return rc;
+  }
+  if (norm_w == nullptr) return PGB_OK;
+  return pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, dtype, stream);
+}
+
+// Largest batch the default exchange mode runs on the fused kernel.
+constexpr int kFusedRowMaxTokens = 256;
+
 }  // namespace pgb
 
 extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_local,
@@ -454,16 +482,10 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
     // split scratch, then fused_add_rmsnorm in place on `out`, beats the fused
     // kernel's grid barrier and row phase here (measured on B200 at T = 1..256:
     // 15.6 vs 18.9 us for o_proj at T = 1, 23.0 vs 29.5 at T = 256).
-    ColScratch sc;
-    sc.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
-    sc.ctr = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kCounters);
-    sc.ctr_bytes = kTileCounterBytes;
-    sc.xchg = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
-    sc.xchg_bytes = kSplitScratchBytes;
-    const int rc = col_gemm_on_scratch(x_local, w_local, bias, out, T, N, K_local, dtype, sc, stream);
-    if (rc || norm_w == nullptr) return rc;
-    return pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, dtype, stream);
+    return row_unfused(comm, x_local, w_local, bias, residual, norm_w, eps, out, T, N, K_local, dtype, stream);
   }
+  if (comm->exchange_mode == PGB_XCHG_AUTO && T > kFusedRowMaxTokens)
+    return row_unfused(comm, x_local, w_local, bias, residual, norm_w, eps, out, T, N, K_local, dtype, stream);
 
   if (comm->exchange_mode == PGB_XCHG_ONESHOT || comm->exchange_mode == PGB_XCHG_TWOSHOT ||
       (comm->exchange_mode == PGB_XCHG_NVLS && comm->nvls)) {
@@ -477,20 +499,9 @@ extern "C" int pgb_row_gemm_allreduce_addnorm(pgb_comm* comm, const void* x_loca
   }
   RowSplit rs;
   if (!plan_rows(comm, T, N, 2, &rs)) {
-    // The payload does not fit the communicator's buffers (the reference
-    // then all-reduces in place, csrc/src/pynccl.cu:127-135): the GEMM into
-    // out, the chunked all-reduce over it, then the fused add + RMSNorm.
-    ColScratch sc;
-    sc.status = reinterpret_cast<int*>(comm->local + LocalLayout::kStatus);
-    sc.ctr = reinterpret_cast<uint32_t*>(comm->local + LocalLayout::kCounters);
-    sc.ctr_bytes = kTileCounterBytes;
-    sc.xchg = reinterpret_cast<float*>(comm->local + LocalLayout::kPartials);
-    sc.xchg_bytes = kSplitScratchBytes;
-    int rc = col_gemm_on_scratch(x_local, w_local, bias, out, T, N, K_local, dtype, sc, stream);
-    if (rc) return rc;
-    rc = pgb_all_reduce(comm, out, static_cast<size_t>(T) * N, dtype, PGB_OP_SUM, stream);
-    if (rc || norm_w == nullptr) return rc;
-    return pgb_fused_add_rmsnorm(out, residual, norm_w, eps, T, N, dtype, stream);
+    // The payload does not fit the communicator's buffers: the chunked
+    // all-reduce of the unfused sequence.
+    return row_unfused(comm, x_local, w_local, bias, residual, norm_w, eps, out, T, N, K_local, dtype, stream);
   }
   const GemmPlan p = plan_gemm(T, N, K_local, comm->sm_count, kSplitScratchBytes);
   if (p.counter_bytes > kTileCounterBytes)

@@ -164,10 +164,13 @@ class PGBCommunicator:
         _lib.call("pgb_comm_set_one_rank_path", self._h, int(bool(fused)))
 
     def set_exchange_mode(self, mode: str) -> None:
-        """Multi-rank decode row ops: "auto" (the default, the grid-barrier
-        kernel), "oneshot" / "twoshot" (the slice-exchange kernel), "barrier",
-        or "nvls" (NVLink multicast reduce; needs a communicator made with
-        nvls=True on hardware that supports it, else "auto")."""
+        """Multi-rank row ops: "auto" (the default: decode batches of up to
+        256 tokens on the grid-barrier kernel, larger batches as the pair-tile
+        column GEMM + all-reduce + fused_add_rmsnorm), "oneshot" / "twoshot"
+        (the slice-exchange kernel), "barrier" (the grid-barrier kernel at
+        every batch size), or "nvls" (NVLink multicast reduce; needs a
+        communicator made with nvls=True on hardware that supports it, else
+        "auto")."""
         codes = {"auto": _lib.PGB_XCHG_AUTO, "oneshot": _lib.PGB_XCHG_ONESHOT, "twoshot": _lib.PGB_XCHG_TWOSHOT,
                  "barrier": _lib.PGB_XCHG_BARRIER, "nvls": _lib.PGB_XCHG_NVLS}
         if mode not in codes:

@@ -138,7 +138,10 @@ def _worker(rank: int, world: int, port: int, case: str, q):
             runs = [(mode, shp) for mode in modes
                     for shp in ((1, 4096, 4096), (8, 4096, 12288), (64, 4096, 4096), (256, 4096, 12288),
                                 (64, 5120, 25600))]
-            runs += [("auto", (1000, 4096, 2048)), ("auto", (3, 200, 256)), ("twoshot", (3, 200, 256))]
+            # A prefill batch: the default mode runs it as the pair-tile GEMM + all-reduce
+            # + norm, the barrier mode on the fused kernel.
+            runs += [("auto", (1000, 4096, 2048)), ("barrier", (1000, 4096, 2048)), ("auto", (3, 200, 256)),
+                     ("twoshot", (3, 200, 256))]
             if comm.nvls:
                 runs += [("nvls", (3, 200, 256))]
             for mode, (T, H, K) in runs:
