@@ -59,10 +59,14 @@ def _within(a, ref, tol=2e-2, ulps=2, extra=None):
 
 def _no_worse_than_reference(mine, ref_path, exact):
     """Error of this kernel against the unrounded f64 result is at most the
-    reference algorithm's own error (plus a quarter of it)."""
+    reference algorithm's own error, plus a quarter of it or half an output
+    ulp at the largest magnitude, whichever is larger: the sums run in other
+    orders (the NVLink switch picks its own), so one element's rounding can
+    land one step away from the reference's."""
     em = (mine.double() - exact).abs().max().item()
     er = (ref_path.double() - exact).abs().max().item()
-    return em <= 1.25 * er + 1e-6, f"err_mine={em:.4g} err_reference={er:.4g}"
+    half_ulp = 0.5 * _ulp(exact.abs().max().reshape(1).to(mine.dtype)).item()
+    return em <= max(1.25 * er, er + half_ulp) + 1e-6, f"err_mine={em:.4g} err_reference={er:.4g}"
 
 
 def _worker(rank: int, world: int, port: int, case: str, q):
