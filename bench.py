@@ -80,6 +80,9 @@ TOKENS = (1, 8, 32, 128, 256)
 HEADLINE_T = 256
 PREFILL_T = 8192
 L2_BYTES = 126 * 2**20
+# DRAM read + write bytes of one gate_up launch (T=256, TP=1) of the single-CTA
+# column kernel, from the ncu capture in profiles/col_gemm_gate_up_T256.md. The
+# bench line reports it as `traffic` only when that kernel runs the shape.
 GATE_UP_T256_TP1_DRAM_BYTES = 207_560_960  # 203.54 MB read + 4.02 MB written (ncu, one launch)
 NVLINK_FALLBACK_GBS = 770.0  # peer copy per direction measured on this pool (profiling recipe)
 
@@ -112,6 +115,24 @@ class Shape:
 
 CFG2 = Shape("config 2", 4096, 12288, 32, 8, 128)
 CFG4 = Shape("config 4", 5120, 25600, 64, 8, 128)
+
+
+def gemm_kernel_name(T: int, N: int, K: int, sms: int = 148) -> str:
+    """The column kernel the library's planner picks for y[T, N] = x . W^T (K
+    inner): the CTA-pair kernels (prefill or 256-token decode tiles) or the
+    single-CTA kernel."""
+    try:
+        import ctypes
+        lib = importlib.import_module("pico-sglang_b200._lib").load()
+        buf = ctypes.create_string_buffer(512)
+        if lib.pgb_describe_plan(T, N, K, sms, 0, 1, buf, 512) != 0:
+            return "col_gemm_kernel"
+        desc = buf.value.decode()
+    except Exception:  # the label only; never fail the bench line over it
+        return "col_gemm_kernel"
+    if "pair=1" in desc:
+        return "col_gemm_pair_swap_kernel" if "swap=1" in desc else "col_gemm_pair_kernel"
+    return "col_gemm_kernel"
 
 
 def load_peaks() -> dict:
@@ -838,6 +859,7 @@ def run_ours(args) -> tuple[dict | None, bool]:
     breakdown = op_breakdown(ctx, L, layers, st, CFG2, T, peaks, nvl)
     gu_us = breakdown["gate_up"]["us"]
     gu_bytes = op_costs(T, n)["gate_up"]["hbm"]
+    gu_kernel = gemm_kernel_name(T, 2 * CFG2.I // n, CFG2.H, torch.cuda.get_device_properties(dev).multi_processor_count)
     achieved = gu_bytes / (gu_us * 1e-6) / 1e9
 
     # End to end through the public API: pinned host inputs copied in, the
@@ -958,16 +980,18 @@ def run_ours(args) -> tuple[dict | None, bool]:
             },
             "tok_per_s_per_layer": head["tok_per_s_per_layer"],
             "roofline": {
-                "kernel": "col_gemm_kernel (gate_up_proj, swap-AB tcgen05)",
+                "kernel": f"{gu_kernel} (gate_up_proj, swap-AB tcgen05)",
                 "bound": "hbm",
                 "achieved": round(achieved, 1),
                 "peak": peaks["hbm_gbs"],
                 "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4),
                 "peak_src": peaks["src"] + " (burst copy bandwidth)",
-                # DRAM read + write bytes of one gate_up launch at T=256, TP=1, from the
-                # ncu capture summarised in profiles/col_gemm_gate_up_T256.md.
-                "traffic": GATE_UP_T256_TP1_DRAM_BYTES if (n == 1 and T == 256) else None,
+                # DRAM read + write bytes of one launch from an ncu capture of this
+                # kernel on this shape, where one exists (see GATE_UP_T256_TP1_DRAM_BYTES).
+                "traffic": GATE_UP_T256_TP1_DRAM_BYTES if (n == 1 and T == 256 and gu_kernel == "col_gemm_kernel")
+                else None,
+                "traffic_single_cta_kernel": GATE_UP_T256_TP1_DRAM_BYTES if (n == 1 and T == 256) else None,
                 "algorithmic_bytes_per_launch": gu_bytes,
                 "avg_launch_us": round(gu_us, 3),
             },
