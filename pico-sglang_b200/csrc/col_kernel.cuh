@@ -634,6 +634,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (threadIdx.x == 0) trace(1001);
 }
 
+// Clusters of two that a pair kernel keeps resident at once on `dev`
+// (cudaOccupancyMaxActiveClusters), queried once per kernel and device.
+template <typename Kern>
+int pair_clusters(Kern kern, const DeviceInfo& dev, int smem_bytes, int* out) {
+  static int cached[64];
+  static bool have[64];
+  if (dev.device >= 0 && dev.device < 64 && have[dev.device]) {
+    *out = cached[dev.device];
+    return PGB_OK;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.gridDim = dim3(2 * (dev.sm_count / 2));
+  cudaLaunchAttribute cl{};
+  cl.id = cudaLaunchAttributeClusterDimension;
+  cl.val.clusterDim.x = 2;
+  cl.val.clusterDim.y = 1;
+  cl.val.clusterDim.z = 1;
+  cfg.attrs = &cl;
+  cfg.numAttrs = 1;
+  int n = 0;
+  PGB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+  if (dev.device >= 0 && dev.device < 64) {
+    cached[dev.device] = n;
+    have[dev.device] = true;
+  }
+  *out = n;
+  return PGB_OK;
+}
+
 // Launch the decode pair kernel for a swap plan with p.pair (counted in
 // pairs). Same arguments as launch_col.
 template <typename IO, typename Epi>
@@ -682,25 +713,17 @@ int launch_col_pair_swap(const GemmPlan& p, const DeviceInfo& dev, const void* x
   g.wait_ns = 2000000000ull;
   g.glu = Epi::kGlu ? 1 : 0;
 
+  int clusters = 0;
+  rc = pair_clusters(kern, dev, L::kBytes, &clusters);
+  if (rc) return rc;
+  // Split partners spin on each other: every pair of the launch must fit at once.
+  if (clusters < p.grid)
+    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d CTA pairs planned, %d fit the device", p.grid, clusters);
   cudaLaunchConfig_t cfg{};
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute cl{};
-  cl.id = cudaLaunchAttributeClusterDimension;
-  cl.val.clusterDim.x = 2;
-  cl.val.clusterDim.y = 1;
-  cl.val.clusterDim.z = 1;
-  cfg.attrs = &cl;
-  cfg.numAttrs = 1;
   cfg.gridDim = dim3(2 * p.grid);
-  int clusters = 0;
-  PGB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
-  // Split partners spin on each other: every pair of the launch must fit at once.
-  if (clusters < p.grid)
-    return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: %d CTA pairs planned, %d fit the device", p.grid, clusters);
-  cfg.attrs = nullptr;
-  cfg.numAttrs = 0;
   return launch_ex(cfg, /*cooperative=*/false, 2, kern, tm_w, tm_x, g, epi);
 }
 
@@ -743,25 +766,16 @@ int launch_col_pair(const GemmPlan& p, const DeviceInfo& dev, const void* x, con
   g.glu = Epi::kGlu ? 1 : 0;
 
   const int pair_tiles = ((T + 2 * kTileP - 1) / (2 * kTileP)) * p.q_tiles;
+  int clusters = 0;
+  rc = pair_clusters(kern, dev, L::kBytes, &clusters);
+  if (rc) return rc;
+  if (clusters < 1) return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: no CTA pair fits an SM pair");
+  clusters = std::min(clusters, std::min(pair_tiles, dev.sm_count / 2));
   cudaLaunchConfig_t cfg{};
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute cl{};
-  cl.id = cudaLaunchAttributeClusterDimension;
-  cl.val.clusterDim.x = 2;
-  cl.val.clusterDim.y = 1;
-  cl.val.clusterDim.z = 1;
-  cfg.attrs = &cl;
-  cfg.numAttrs = 1;
-  cfg.gridDim = dim3(2 * (dev.sm_count / 2));
-  int clusters = 0;
-  PGB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
-  if (clusters < 1) return set_error(PGB_ERR_UNSUPPORTED, "col_gemm: no CTA pair fits an SM pair");
-  clusters = std::min(clusters, std::min(pair_tiles, dev.sm_count / 2));
   cfg.gridDim = dim3(2 * clusters);
-  cfg.attrs = nullptr;
-  cfg.numAttrs = 0;
   return launch_ex(cfg, /*cooperative=*/false, 2, kern, tm_x, tm_w, g, epi);
 }
 
@@ -832,8 +846,15 @@ int launch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const vo
 template <typename IO, typename Epi>
 int dispatch_col(const GemmPlan& p, const DeviceInfo& dev, const void* x, const void* w, int T, int N, int K,
                  const ColScratch& sc, cudaStream_t stream, const Epi& epi) {
-  if (!p.swap && p.pair) return launch_col_pair<IO>(p, dev, x, w, T, N, K, sc, stream, epi);
-  if (p.swap && p.pair) return launch_col_pair_swap<IO>(p, dev, x, w, T, N, K, sc, stream, epi);
+  if (p.pair) {
+    const int rc = p.swap ? launch_col_pair_swap<IO>(p, dev, x, w, T, N, K, sc, stream, epi)
+                          : launch_col_pair<IO>(p, dev, x, w, T, N, K, sc, stream, epi);
+    if (rc != PGB_ERR_UNSUPPORTED) return rc;
+    // The device cannot keep the pairs resident: the single-CTA plan.
+    GemmPlan q = plan_gemm(T, Epi::kGlu ? 2 * N : N, K, dev.sm_count, sc.xchg_bytes);
+    q.pair = false;
+    return dispatch_col<IO>(q, dev, x, w, T, N, K, sc, stream, epi);
+  }
   if (!p.swap) return launch_col<IO, 256, false>(p, dev, x, w, T, N, K, sc, stream, epi);
   switch (p.bn) {
     case 32: return launch_col<IO, 32, true>(p, dev, x, w, T, N, K, sc, stream, epi);
