@@ -176,3 +176,30 @@ def test_rope_store_rejects_mixed_dtypes_before_launch(pgb):
     with pytest.raises(TypeError, match="status"):
         pgb.ops.rope_store(qkv, idx, idx, table, 1, 1, 128, kc.float(), kc.float(),
                            status=torch.zeros(1, dtype=torch.int64))
+
+
+def _plan(lib, T, N, K, sms=148, fused_row=0):
+    import ctypes
+
+    buf = ctypes.create_string_buffer(512)
+    assert lib.pgb_describe_plan(T, N, K, sms, fused_row, 1, buf, 512) == 0
+    return dict(kv.split("=") for kv in buf.value.decode().split())
+
+
+def test_cta_pair_plans(pgb):
+    """Column kernels run prefill shapes (T > 256) and 129-256-token decode
+    batches on CTA pairs; shorter batches and the row-parallel kernels keep
+    single-CTA tiles; the pair decompositions cover every k-block once."""
+    lib = pgb._lib.load()
+    p = _plan(lib, 8192, 24576, 4096)
+    assert (p["swap"], p["pair"]) == ("0", "1")
+    p = _plan(lib, 256, 24576, 4096)
+    assert (p["swap"], p["pair"], p["bn"]) == ("1", "1", "256")
+    assert int(p["grid"]) <= 148 // 2  # pairs
+    for T in (1, 8, 64, 128):
+        assert _plan(lib, T, 4096, 4096)["pair"] == "0"
+    assert _plan(lib, 256, 4096, 4096, fused_row=1)["pair"] == "0"
+    for sms in (148, 132, 100):
+        for T in (129, 200, 256):
+            for N, K in ((512, 256), (768, 4096), (3072, 4096), (4096, 12288), (24576, 4096), (12800, 5120)):
+                assert lib.pgb_check_work_plan(T, N, K, sms, 0, 0, 1) == 0, (T, N, K, sms, lib.pgb_last_error())
