@@ -70,8 +70,10 @@ def test_col_gemm_matches_f32(pgb, cuda_device, T, N, K, dtype):
 
 
 def test_col_gemm_fp16_and_bias(pgb, cuda_device):
+    """fp16 with a bias on each kernel: single-CTA decode (T = 4), the decode
+    CTA-pair kernel (T = 200) and the prefill CTA-pair kernel (T = 300)."""
     g = torch.Generator(device=cuda_device).manual_seed(7)
-    for T in (4, 300):
+    for T in (4, 200, 300):
         x = torch.randn(T, 512, device=cuda_device, generator=g).half()
         w = (torch.randn(1024, 512, device=cuda_device, generator=g) * 0.02).half()
         b = torch.randn(1024, device=cuda_device, generator=g).half()
