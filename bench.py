@@ -1085,6 +1085,10 @@ def _config1_rank(rank: int, port: int, threads: int, budget_s: float, q) -> Non
 
     import oracle
 
+    # Under torchrun this process inherits the elastic agent's store setting,
+    # which would make both ranks clients of a store nobody serves: the pair
+    # below has its own rendezvous.
+    os.environ.pop("TORCHELASTIC_USE_AGENT_STORE", None)
     torch.set_num_threads(threads)
     dist.init_process_group("gloo", rank=rank, world_size=2, init_method=f"tcp://127.0.0.1:{port}",
                             timeout=timedelta(seconds=120))
